@@ -1,0 +1,176 @@
+// Mask semantics shared by every attention kernel.
+//
+// The flattened mask (attn_mask_t) reproduces the reference's composed
+// ScoreMods (attnax/kernels/score_mods.py) and `mask=` argument:
+//   causal_mod          keep kv <= q                    (score_mods.py:100-102)
+//   sliding_window_mod  keep kv <= q and q - kv < W      (:139-141), or |q-kv| < W (:142)
+//   prefix_lm_mod       keep kv < prefix[b] or kv <= q   (:171-174)
+//   document_mask_mod   keep ids[b,q] == ids[b,kv]       (:195-209)
+//   alibi_mod           s - slope[h] * |q - kv|          (:76-79)
+//   additive_bias_mod   s + bias                         (:235)
+//   mask=               where(mask, s, finfo.min)        (attention.py:60-62)
+// Dropped scores become -FLT_MAX in the log2 domain (the reference's
+// finfo.min), so a row with nothing kept still averages V uniformly; key
+// columns past the end of the sequence are -inf and never count.
+#pragma once
+#include <cfloat>
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "../../include/attnb200.h"
+
+namespace attnb200 {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+enum TileState : int { kSkip = 0, kPartial = 1, kFull = 2 };
+
+// Tile size of the document-id range tables (both q and kv tiles).
+constexpr int kDocTile = 128;
+
+__host__ __device__ inline long long ll_min(long long a, long long b) { return a < b ? a : b; }
+__host__ __device__ inline long long ll_max(long long a, long long b) { return a > b ? a : b; }
+
+// Classifies the tile [q0,q1) x [k0,k1) of batch b (local positions).
+// doc_q_tiles/doc_kv_tiles hold (min,max) ids per kDocTile-row tile; when
+// they are null a document mask makes every tile partial.
+__host__ __device__ inline int tile_state(const attn_mask_t& m, const int2* doc_q_tiles,
+                                          const int2* doc_kv_tiles, int nq_doc, int nk_doc, int b,
+                                          int q0, int q1, int k0, int k1, int bn) {
+  int st = kFull;
+  if (k1 - k0 < bn) st = kPartial;
+  const long long qlo = m.q_offset + q0, qhi = m.q_offset + q1 - 1;
+  const long long klo = m.kv_offset + k0, khi = m.kv_offset + k1 - 1;
+  if (m.has_band) {
+    const long long dmin = qlo - khi, dmax = qhi - klo;
+    if (dmax < m.band_lo || dmin > m.band_hi) return kSkip;
+    if (!(dmin >= m.band_lo && dmax <= m.band_hi)) st = kPartial;
+  }
+  if (m.prefix_len) {
+    const long long pref = m.prefix_len[b];
+    if (klo >= pref && klo > qhi) return kSkip;
+    if (!(khi < pref || khi <= qlo)) st = kPartial;
+  }
+  if (m.doc_q) {
+    if (doc_q_tiles && doc_kv_tiles && (q0 % kDocTile) == 0 && (k0 % kDocTile) == 0 &&
+        q1 - q0 <= kDocTile && k1 - k0 <= kDocTile) {
+      const int2 a = doc_q_tiles[(long long)b * nq_doc + q0 / kDocTile];
+      const int2 c = doc_kv_tiles[(long long)b * nk_doc + k0 / kDocTile];
+      if (a.y < c.x || c.y < a.x) return kSkip;
+      if (!(a.x == a.y && c.x == c.y && a.x == c.x)) st = kPartial;
+    } else {
+      st = kPartial;
+    }
+  }
+  if (m.bool_mask || m.bias) st = kPartial;
+  return st;
+}
+
+// Local kv-tile index range [lo, hi) that the band allows for rows [q0, q1).
+__host__ __device__ inline void band_tile_range(const attn_mask_t& m, int q0, int q1, int seq_kv,
+                                                int bn, int* lo, int* hi) {
+  const int nk = (seq_kv + bn - 1) / bn;
+  *lo = 0;
+  *hi = nk;
+  if (m.has_band) {
+    const long long qlo = m.q_offset + q0, qhi = m.q_offset + q1 - 1;
+    long long c_lo = qlo - m.band_hi - m.kv_offset;   // smallest local kv col kept
+    long long c_hi = qhi - m.band_lo - m.kv_offset;   // largest
+    c_lo = ll_max(c_lo, 0);
+    c_hi = ll_min(c_hi, (long long)seq_kv - 1);
+    if (c_hi < c_lo) {
+      *lo = *hi = 0;
+      return;
+    }
+    *lo = (int)(c_lo / bn);
+    *hi = (int)(c_hi / bn) + 1;
+  }
+}
+
+__device__ __forceinline__ float load_bias(const void* p, attn_dtype_t dt, long long idx) {
+  if (dt == ATTN_F32) return __ldg(reinterpret_cast<const float*>(p) + idx);
+  if (dt == ATTN_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
+  return __half2float(reinterpret_cast<const __half*>(p)[idx]);
+}
+
+// Element transform for one score: raw q.k -> log2-domain score t, with
+// every mask and additive term.  `row`/`col` are local positions.
+__device__ __forceinline__ float mask_score(const attn_mask_t& m, float raw, float sl2,
+                                            float slope_l2, int b, int h, int row, int col,
+                                            int seq_kv, bool partial) {
+  const long long qg = m.q_offset + row, kvg = m.kv_offset + col;
+  float t = raw * sl2;
+  if (m.alibi_slopes) t -= slope_l2 * fabsf((float)(int)(qg - kvg));
+  if (!partial) return t;
+  if (col >= seq_kv) return -INFINITY;
+  bool keep = true;
+  if (m.has_band) {
+    const long long d = qg - kvg;
+    keep = keep && d >= m.band_lo && d <= m.band_hi;
+  }
+  if (m.prefix_len) keep = keep && (kvg < (long long)m.prefix_len[b] || kvg <= qg);
+  if (m.doc_q)
+    keep = keep && (__ldg(m.doc_q + (long long)b * m.doc_q_bstride + qg) ==
+                    __ldg(m.doc_kv + (long long)b * m.doc_kv_bstride + kvg));
+  if (m.bool_mask)
+    keep = keep && m.bool_mask[b * m.mask_strides[0] + h * m.mask_strides[1] +
+                               row * m.mask_strides[2] + col * m.mask_strides[3]] != 0;
+  if (m.bias)
+    t += kLog2e * load_bias(m.bias, m.bias_dtype,
+                            b * m.bias_strides[0] + h * m.bias_strides[1] +
+                                row * m.bias_strides[2] + col * m.bias_strides[3]);
+  return keep ? t : -FLT_MAX;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// (min, max) of document ids over kDocTile-row tiles of global positions
+// offset + [t*kDocTile, min((t+1)*kDocTile, len)).
+__global__ void doc_tile_range_kernel(const int32_t* ids, long long bstride, long long offset,
+                                      int len, int ntiles, int2* out) {
+  const int t = blockIdx.x, b = blockIdx.y;
+  int lo = 0x7fffffff, hi = -0x7fffffff - 1;
+  for (int i = t * kDocTile + threadIdx.x; i < min((t + 1) * kDocTile, len); i += blockDim.x) {
+    const int v = ids[(long long)b * bstride + offset + i];
+    lo = min(lo, v);
+    hi = max(hi, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  __shared__ int slo[32], shi[32];
+  const int w = threadIdx.x / 32;
+  if ((threadIdx.x & 31) == 0) {
+    slo[w] = lo;
+    shi[w] = hi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < (int)blockDim.x / 32; ++i) {
+      lo = min(lo, slo[i]);
+      hi = max(hi, shi[i]);
+    }
+    out[(long long)b * ntiles + t] = make_int2(lo, hi);
+  }
+}
+
+}  // namespace attnb200

@@ -1,0 +1,171 @@
+/*
+ * attnb200 — C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Plain C: device pointers, element strides, sizes, and CUDA streams passed
+ * as `void*` (a `cudaStream_t`).  Every entry point returns an attn_status_t
+ * (0 = success) and never allocates device memory: work buffers come from
+ * the caller through `workspace`, sized by the matching *_workspace_size().
+ * Tensors use the reference's (batch, heads, seq, head_dim) layout with a
+ * unit stride on head_dim; the other strides are free but must be multiples
+ * of 16 bytes for the tensor-core paths.
+ *
+ * Reference interfaces replaced (attnax, paths inside the project):
+ *   attn_fwd            flash_attention / pallas_flash_attention /
+ *                       memory_efficient_attention / standard_attention
+ *                       (attnax/kernels/attention.py:17-283,
+ *                        attnax/kernels/pallas.py:27-244), forward
+ *   attn_bwd            JAX autodiff of the same functions (the reference
+ *                       has no hand-written backward; pallas.py:45-47)
+ *   attn_paged_decode   paged_attention (attnax/kernels/paged.py:17-84) over
+ *                       PagedKVCache block tables (attnax/paged_cache.py:12-48)
+ *   attn_paged_gather   gather_kv (attnax/paged_cache.py:201-231)
+ *   attn_paged_append   append_kv (attnax/paged_cache.py:144-198)
+ *   attn_ring_fwd       ring_attention (attnax/kernels/attention.py:540-691),
+ *                       the lax.ppermute ring (:673-674) done with NCCL
+ *   attn_comm_*         the device-axis binding that jax.lax.axis_index /
+ *                       axis_size (:604-617) provide in the reference
+ */
+#ifndef ATTNB200_H_
+#define ATTNB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  ATTN_OK = 0,
+  ATTN_ERR_INVALID = 1,      /* bad shape, stride, alignment or pointer */
+  ATTN_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement */
+  ATTN_ERR_CUDA = 3,         /* a CUDA runtime call failed */
+  ATTN_ERR_NCCL = 4,         /* an NCCL call failed or the communicator broke */
+  ATTN_ERR_WORKSPACE = 5,    /* workspace missing or too small */
+  ATTN_ERR_TIMEOUT = 6       /* a bounded device wait gave up (see attn_device_status) */
+} attn_status_t;
+
+typedef enum { ATTN_F32 = 0, ATTN_BF16 = 1, ATTN_F16 = 2 } attn_dtype_t;
+
+/*
+ * Flattened score modification: the built-in ScoreMods of
+ * attnax/kernels/score_mods.py composed left to right
+ * (attnax/kernels/_api.py:166-196) plus the boolean `mask=` argument.
+ * Selections AND together; additive terms sum.  An entry is kept iff
+ *   band_lo <= q - kv <= band_hi                        (has_band)
+ *   and (kv < prefix_len[b] or kv <= q)                 (prefix_len)
+ *   and doc_q[b, q] == doc_kv[b, kv]                    (doc_q, doc_kv)
+ *   and bool_mask[b, h, q, kv] != 0                     (bool_mask)
+ * where q, kv are global positions (row + q_offset, col + kv_offset).
+ * A dropped entry gets the score finfo(float32).min, as in the reference.
+ * Kept scores are  s = scale * q.k - alibi_slopes[h] * |q - kv| + bias[...].
+ */
+typedef struct {
+  int32_t has_band;
+  int64_t band_lo, band_hi;
+  const int32_t* prefix_len;     /* [batch] or NULL */
+  const int32_t* doc_q;          /* [batch, *] ids indexed by global q, or NULL */
+  const int32_t* doc_kv;         /* [batch, *] ids indexed by global kv */
+  int64_t doc_q_bstride, doc_kv_bstride;
+  const float* alibi_slopes;     /* [num_heads_q] or NULL */
+  const void* bias;              /* broadcastable (b, h, q, kv) or NULL */
+  attn_dtype_t bias_dtype;
+  int64_t bias_strides[4];       /* element strides, 0 where broadcast */
+  const uint8_t* bool_mask;      /* broadcastable (b, h, q, kv) or NULL */
+  int64_t mask_strides[4];
+  int64_t q_offset, kv_offset;   /* global position of local row/col 0 */
+} attn_mask_t;
+
+typedef struct {
+  attn_dtype_t dtype;            /* of q, k, v, out */
+  int32_t batch, num_heads_q, num_heads_kv, seq_q, seq_kv, head_dim;
+  const void* q; const void* k; const void* v; void* out;
+  int64_t q_strides[3], k_strides[3], v_strides[3], o_strides[3]; /* b, h, s */
+  float* lse;                    /* [batch, heads_q, seq_q] natural log, or NULL */
+  float softmax_scale;           /* rsqrt(head_dim) for the reference */
+  int32_t fix_masked_rows;       /* 1: rows with no kept key average all of V */
+  attn_mask_t mask;
+  void* workspace; size_t workspace_bytes;
+} attn_fwd_params_t;
+
+typedef struct {
+  attn_dtype_t dtype;
+  int32_t batch, num_heads_q, num_heads_kv, seq_q, seq_kv, head_dim;
+  const void* q; const void* k; const void* v; const void* out; const void* d_out;
+  const float* lse;              /* from attn_fwd */
+  void* dq; void* dk; void* dv;  /* same layout/dtype as q, k, v */
+  int64_t q_strides[3], k_strides[3], v_strides[3], o_strides[3], do_strides[3];
+  int64_t dq_strides[3], dk_strides[3], dv_strides[3];
+  float softmax_scale;
+  int32_t fix_masked_rows;       /* 1: rows with no kept key add dO/seq_kv to all of dV */
+  attn_mask_t mask;
+  void* workspace; size_t workspace_bytes;
+} attn_bwd_params_t;
+
+typedef struct {
+  attn_dtype_t dtype;
+  int32_t num_seqs, num_heads_q, num_heads_kv, head_dim, seq_q;
+  int32_t num_blocks, block_size, max_blocks_per_seq;
+  int32_t max_context;           /* upper bound of seq_lengths, for split planning */
+  const void* q;                 /* [num_seqs, heads_q, seq_q, head_dim] contiguous */
+  const void* key_pool;          /* [num_blocks, block_size, heads_kv, head_dim] */
+  const void* value_pool;
+  const int32_t* block_table;    /* [num_seqs, max_blocks_per_seq], -1 unused */
+  const int32_t* seq_lengths;    /* [num_seqs] */
+  void* out;                     /* like q */
+  float softmax_scale;
+  void* workspace; size_t workspace_bytes;
+} attn_paged_params_t;
+
+typedef struct {
+  attn_dtype_t dtype;
+  int32_t batch, num_heads_q, num_heads_kv, seq_local, head_dim;
+  const void* q; const void* k; const void* v; void* out;   /* contiguous local shards */
+  float* lse;                    /* [batch, heads_q, seq_local] or NULL */
+  float softmax_scale;
+  int32_t causal;                /* causal_mod with global positions */
+  int32_t balance;               /* 1: zig-zag re-sharding for causal load balance */
+  void* workspace; size_t workspace_bytes;
+} attn_ring_params_t;
+
+/* ---- flash attention ---------------------------------------------------- */
+size_t attn_fwd_workspace_size(const attn_fwd_params_t* p);
+int attn_fwd(const attn_fwd_params_t* p, void* stream);
+size_t attn_bwd_workspace_size(const attn_bwd_params_t* p);
+int attn_bwd(const attn_bwd_params_t* p, void* stream);
+
+/* ---- paged KV cache ----------------------------------------------------- */
+size_t attn_paged_decode_workspace_size(const attn_paged_params_t* p);
+int attn_paged_decode(const attn_paged_params_t* p, void* stream);
+/* Contiguous copy of sequence `seq`: keys/values [seq_len, heads_kv, head_dim]. */
+int attn_paged_gather(attn_dtype_t dtype, const void* key_pool, const void* value_pool,
+                      int32_t block_size, int32_t heads_kv, int32_t head_dim,
+                      const int32_t* block_table_row, int32_t seq_len,
+                      void* keys_out, void* values_out, void* stream);
+/* Writes `chunk` new tokens of sequence `seq` at positions start.. (block
+ * table already populated; -1 slots are reported through `bad_slot`). */
+int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool,
+                      int32_t block_size, int32_t heads_kv, int32_t head_dim,
+                      const int32_t* block_table_row, int32_t start, int32_t chunk,
+                      const void* keys_new, const void* values_new,
+                      int32_t* bad_slot, void* stream);
+
+/* ---- ring attention over NCCL -------------------------------------------- */
+int attn_comm_unique_id(void* out, size_t out_bytes);       /* 128 bytes */
+int attn_comm_init(const void* unique_id, int32_t nranks, int32_t rank, void** comm);
+int attn_comm_destroy(void* comm);
+size_t attn_ring_workspace_size(const attn_ring_params_t* p, int32_t nranks);
+int attn_ring_fwd(const attn_ring_params_t* p, void* comm, void* compute_stream,
+                  void* comm_stream);
+
+/* ---- diagnostics -------------------------------------------------------- */
+/* Reads and clears the device status word that bounded waits set on
+ * timeout (0 = none).  Synchronises the current device. */
+int attn_device_status(int32_t* status);
+const char* attn_status_string(int status);
+int attn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATTNB200_H_ */

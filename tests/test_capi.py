@@ -1,0 +1,70 @@
+"""The C-ABI library loads and exports every symbol the public header declares (no GPU)."""
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+from attnax_b200 import _lib
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+
+
+def header_functions():
+    text = (ROOT / "include" / "attnb200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(attn_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    names = header_functions()
+    for n in ("attn_fwd", "attn_bwd", "attn_paged_decode", "attn_paged_gather", "attn_paged_append",
+              "attn_ring_fwd", "attn_comm_init", "attn_comm_destroy"):
+        assert n in names
+
+
+def test_library_loads_and_exports_every_header_symbol():
+    if not pathlib.Path(_lib.LIB_PATH).exists():
+        pytest.fail("libattnb200.so is not built; run __graft_entry__.build()")
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for n in header_functions():
+        assert hasattr(lib, n), f"{n} missing from {_lib.LIB_PATH}"
+    assert set(header_functions()) == set(_lib.SIGNATURES), "ctypes signatures out of sync with header"
+    assert _lib.load().attn_version() >= 1
+    assert _lib.load().attn_status_string(2) == b"unsupported configuration"
+
+
+def test_struct_sizes_are_stable():
+    # The ctypes mirrors must match the C layout the library was compiled with.
+    assert ctypes.sizeof(_lib.AttnMask) % 8 == 0
+    assert ctypes.sizeof(_lib.FwdParams) > ctypes.sizeof(_lib.AttnMask)
+
+
+def test_ctypes_layout_matches_c_compiler(tmp_path):
+    """Offsets and sizes of the ctypes mirrors equal what gcc computes from the header."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    structs = {"attn_mask_t": _lib.AttnMask, "attn_fwd_params_t": _lib.FwdParams,
+               "attn_bwd_params_t": _lib.BwdParams, "attn_paged_params_t": _lib.PagedParams,
+               "attn_ring_params_t": _lib.RingParams}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{ROOT}/include/attnb200.h"',
+             "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname}.{fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
+    got = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                 check=True).stdout.splitlines())
+    for cname, py in structs.items():
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert int(got[f"{cname}.{fname}"]) == getattr(py, fname).offset, f"{cname}.{fname}"
