@@ -96,6 +96,7 @@ SIGNATURES = {
     "attn_device_status": (C.c_int, [C.POINTER(i32)]),
     "attn_status_string": (C.c_char_p, [C.c_int]),
     "attn_version": (C.c_int, []),
+    "attn_launch_count": (C.c_uint64, []),
 }
 
 _lock = threading.Lock()

@@ -174,3 +174,132 @@ __global__ void doc_tile_range_kernel(const int32_t* ids, long long bstride, lon
 }
 
 }  // namespace attnb200
+
+namespace attnb200 {
+
+// Per-thread constants for transforming one row of a score tile held in
+// registers.  Columns are kv positions (forward, dQ) or q positions
+// (dK/dV, "transposed").  d(c) = q - kv at column c = d0 + dstep * c.
+struct RowCtx {
+  float sl2;        // softmax scale * log2(e)
+  float slope_l2;   // ALiBi slope * log2(e) (0 when no ALiBi)
+  int d0, dstep;
+  int ncols;        // columns < ncols are inside the sequence
+  int band_lo, band_hi;
+  int pref_cols;    // prefix: columns c < pref_cols are kept regardless of d (see make_row_ctx)
+  int doc_fixed;    // document id of this row
+  const int32_t* doc_cols;  // document ids indexed by column
+  const uint8_t* bmask;     // bool mask at column 0, column stride bmask_cs
+  long long bmask_cs;
+  const void* bias;         // bias at column 0, column stride bias_cs
+  long long bias_cs;
+  attn_dtype_t bias_dtype;
+  bool alibi, band, prefix, doc;
+};
+
+__device__ __forceinline__ int clamp_i32(long long x) {
+  return (int)(x < -(1ll << 30) ? -(1ll << 30) : (x > (1ll << 30) ? (1ll << 30) : x));
+}
+
+// row/col0 are local positions of this thread's row and of column 0.
+// transposed: the row is a kv position and columns are q positions.
+__device__ __forceinline__ RowCtx make_row_ctx(const attn_mask_t& m, float sl2, int b, int hq,
+                                               int row, int col0, int ncols, bool transposed) {
+  RowCtx r;
+  r.sl2 = sl2;
+  r.alibi = m.alibi_slopes != nullptr;
+  r.slope_l2 = r.alibi ? m.alibi_slopes[hq] * kLog2e : 0.f;
+  const long long qg0 = m.q_offset + (transposed ? col0 : row);
+  const long long kg0 = m.kv_offset + (transposed ? row : col0);
+  r.d0 = clamp_i32(qg0 - kg0);
+  r.dstep = transposed ? 1 : -1;
+  r.ncols = ncols;
+  r.band = m.has_band != 0;
+  r.band_lo = clamp_i32(m.has_band ? m.band_lo : -(1ll << 40));
+  r.band_hi = clamp_i32(m.has_band ? m.band_hi : (1ll << 40));
+  r.prefix = m.prefix_len != nullptr;
+  r.pref_cols = 0;
+  if (r.prefix) {
+    const long long pref = m.prefix_len[b];
+    // kept when kv < pref: forward columns c < pref - kg0; transposed: all or none
+    r.pref_cols = transposed ? (kg0 < pref ? (1 << 30) : 0) : clamp_i32(pref - kg0);
+  }
+  r.doc = m.doc_q != nullptr;
+  r.doc_fixed = 0;
+  r.doc_cols = nullptr;
+  if (r.doc) {
+    if (transposed) {
+      r.doc_fixed = m.doc_kv[(long long)b * m.doc_kv_bstride + kg0];
+      r.doc_cols = m.doc_q + (long long)b * m.doc_q_bstride + qg0;
+    } else {
+      r.doc_fixed = m.doc_q[(long long)b * m.doc_q_bstride + qg0];
+      r.doc_cols = m.doc_kv + (long long)b * m.doc_kv_bstride + kg0;
+    }
+  }
+  const int qrow = transposed ? col0 : row, kcol = transposed ? row : col0;
+  r.bmask = nullptr;
+  r.bmask_cs = 0;
+  if (m.bool_mask) {
+    r.bmask = m.bool_mask + b * m.mask_strides[0] + hq * m.mask_strides[1] +
+              (long long)qrow * m.mask_strides[2] + (long long)kcol * m.mask_strides[3];
+    r.bmask_cs = transposed ? m.mask_strides[2] : m.mask_strides[3];
+  }
+  r.bias = nullptr;
+  r.bias_cs = 0;
+  r.bias_dtype = m.bias_dtype;
+  if (m.bias) {
+    const long long off = b * m.bias_strides[0] + hq * m.bias_strides[1] +
+                          (long long)qrow * m.bias_strides[2] + (long long)kcol * m.bias_strides[3];
+    const int es = m.bias_dtype == ATTN_F32 ? 4 : 2;
+    r.bias = reinterpret_cast<const char*>(m.bias) + off * es;
+    r.bias_cs = transposed ? m.bias_strides[2] : m.bias_strides[3];
+  }
+  return r;
+}
+
+// Raw q.k scores -> log2-domain masked scores, for N register-resident
+// columns.  Each feature is its own branch-free unrolled loop so the common
+// (full-tile) path stays short.
+template <int N>
+__device__ __forceinline__ void transform_row(float (&s)[N], const RowCtx& r, bool partial) {
+  if (r.alibi) {
+    const float fd0 = (float)r.d0, fstep = (float)r.dstep;
+#pragma unroll
+    for (int c = 0; c < N; ++c) s[c] = fmaf(-r.slope_l2, fabsf(fmaf(fstep, (float)c, fd0)), s[c] * r.sl2);
+  } else {
+#pragma unroll
+    for (int c = 0; c < N; ++c) s[c] *= r.sl2;
+  }
+  if (!partial) return;
+  if (r.bias) {
+    if (r.bias_dtype == ATTN_F32) {
+      const float* p = reinterpret_cast<const float*>(r.bias);
+#pragma unroll
+      for (int c = 0; c < N; ++c)
+        if (c < r.ncols) s[c] = fmaf(kLog2e, __ldg(p + c * r.bias_cs), s[c]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < N; ++c)
+        if (c < r.ncols) s[c] = fmaf(kLog2e, load_bias(r.bias, r.bias_dtype, c * r.bias_cs), s[c]);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < N; ++c) {
+    const int d = r.d0 + r.dstep * c;
+    bool keep = !r.band || (d >= r.band_lo && d <= r.band_hi);
+    if (r.prefix) keep = keep && (c < r.pref_cols || d >= 0);
+    s[c] = c < r.ncols ? (keep ? s[c] : -FLT_MAX) : -INFINITY;
+  }
+  if (r.doc) {
+#pragma unroll
+    for (int c = 0; c < N; ++c)
+      if (c < r.ncols && __ldg(r.doc_cols + c) != r.doc_fixed) s[c] = -FLT_MAX;
+  }
+  if (r.bmask) {
+#pragma unroll
+    for (int c = 0; c < N; ++c)
+      if (c < r.ncols && r.bmask[c * r.bmask_cs] == 0) s[c] = -FLT_MAX;
+  }
+}
+
+}  // namespace attnb200

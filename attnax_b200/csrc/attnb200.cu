@@ -5,12 +5,14 @@
 
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/attnb200.h"
 #include "attn_common.cuh"
 #include "flash_fwd_sm100.cu"
 #include "flash_simt.cu"
+#include "flash_bwd_sm100.cu"
 #include "paged.cu"
 #include "ring.cu"
 
@@ -130,7 +132,11 @@ static bool check_mask(const attn_mask_t& m, int B) {
   return true;
 }
 
-static int launch_status() {
+static std::atomic<unsigned long long> g_launches{0};
+
+// Counts `n` kernel launches and reports the launch error state.
+static int launch_status(int n = 1) {
+  g_launches.fetch_add(n, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     fprintf(stderr, "attnb200: CUDA launch error: %s\n", cudaGetErrorString(e));
@@ -240,6 +246,8 @@ extern "C" {
 
 int attn_version(void) { return 1; }
 
+uint64_t attn_launch_count(void) { return g_launches.load(); }
+
 const char* attn_status_string(int s) {
   switch (s) {
     case ATTN_OK: return "ok";
@@ -291,6 +299,8 @@ int attn_fwd(const attn_fwd_params_t* p, void* stream) {
                                                                p->mask.q_offset, p->seq_q, nq, dq_t);
     doc_tile_range_kernel<<<dim3(nk, p->batch), 128, 0, st>>>(
         p->mask.doc_kv, p->mask.doc_kv_bstride, p->mask.kv_offset, p->seq_kv, nk, dkv_t);
+    const int lrc = launch_status(2);
+    if (lrc != ATTN_OK) return lrc;
   }
   int rc;
   if (tc) {
@@ -326,9 +336,82 @@ int attn_fwd(const attn_fwd_params_t* p, void* stream) {
   return rc;
 }
 
+}  // extern "C"
+
+namespace attnb200 {
+static bool bwd_tc_ok(const attn_bwd_params_t* p) {
+  if (p->dtype == ATTN_F32 || (p->head_dim != 64 && p->head_dim != 128)) return false;
+  const void* ptrs[9] = {p->q, p->k, p->v, p->out, p->d_out, p->dq, p->dk, p->dv, p->lse};
+  for (auto* x : ptrs)
+    if (reinterpret_cast<uintptr_t>(x) % 16) return false;
+  const int64_t* ss[8] = {p->q_strides, p->k_strides, p->v_strides, p->o_strides, p->do_strides,
+                          p->dq_strides, p->dk_strides, p->dv_strides};
+  for (auto* s : ss)
+    for (int i = 0; i < 3; ++i)
+      if (s[i] % 8) return false;
+  return true;
+}
+
+static int bwd_seq_pad(const attn_bwd_params_t* p) { return (p->seq_q + 127) / 128 * 128; }
+
+template <int D, bool BF16>
+static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse2, cudaStream_t st) {
+  using namespace bwd;
+  const int Sq_pad = bwd_seq_pad(p);
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  prep_pad_kernel<T><<<dim3(Sq_pad / 4, p->num_heads_q, p->batch), 128, 0, st>>>(
+      reinterpret_cast<const T*>(p->out), reinterpret_cast<const T*>(p->d_out), p->o_strides[0],
+      p->o_strides[1], p->o_strides[2], p->do_strides[0], p->do_strides[1], p->do_strides[2], p->lse,
+      delta, lse2, p->num_heads_q, p->seq_q, Sq_pad, D);
+  Args a;
+  a.B = p->batch; a.Hq = p->num_heads_q; a.Hkv = p->num_heads_kv; a.Sq = p->seq_q; a.Skv = p->seq_kv;
+  a.Sq_pad = Sq_pad; a.group = p->num_heads_q / p->num_heads_kv;
+  a.sl2 = p->softmax_scale * kLog2e; a.scale = p->softmax_scale;
+  a.lse2 = lse2; a.delta = delta;
+  a.dq = p->dq; a.dk = p->dk; a.dv = p->dv;
+  for (int i = 0; i < 3; ++i) {
+    a.dq_s[i] = p->dq_strides[i]; a.dk_s[i] = p->dk_strides[i]; a.dv_s[i] = p->dv_strides[i];
+  }
+  a.mask = p->mask;
+  CUtensorMap q64, do64, k128, v128, q128, do128, k64, v64;
+  const int B = p->batch, Hq = p->num_heads_q, Hkv = p->num_heads_kv, Sq = p->seq_q, Skv = p->seq_kv;
+  if (!make_tmap(&q64, p->dtype, p->q, B, Hq, Sq, D, p->q_strides, QT) ||
+      !make_tmap(&do64, p->dtype, p->d_out, B, Hq, Sq, D, p->do_strides, QT) ||
+      !make_tmap(&k128, p->dtype, p->k, B, Hkv, Skv, D, p->k_strides, KROWS) ||
+      !make_tmap(&v128, p->dtype, p->v, B, Hkv, Skv, D, p->v_strides, KROWS) ||
+      !make_tmap(&q128, p->dtype, p->q, B, Hq, Sq, D, p->q_strides, QROWS) ||
+      !make_tmap(&do128, p->dtype, p->d_out, B, Hq, Sq, D, p->do_strides, QROWS) ||
+      !make_tmap(&k64, p->dtype, p->k, B, Hkv, Skv, D, p->k_strides, KT) ||
+      !make_tmap(&v64, p->dtype, p->v, B, Hkv, Skv, D, p->v_strides, KT))
+    return ATTN_ERR_INVALID;
+  auto kkv = dkdv_kernel<D, BF16>;
+  auto kq = dq_kernel<D, BF16>;
+  static int attr_dev_kv = -1, attr_dev_q = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev_kv != dev) {
+    if (cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgKV<D>::SMEM) != cudaSuccess)
+      return ATTN_ERR_CUDA;
+    attr_dev_kv = dev;
+  }
+  if (attr_dev_q != dev) {
+    if (cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgQ<D>::SMEM) != cudaSuccess)
+      return ATTN_ERR_CUDA;
+    attr_dev_q = dev;
+  }
+  kkv<<<dim3((Skv + KROWS - 1) / KROWS, Hkv, B), kThreads, CfgKV<D>::SMEM, st>>>(q64, k128, v128, do64, a);
+  kq<<<dim3((Sq + QROWS - 1) / QROWS, Hq, B), kThreads, CfgQ<D>::SMEM, st>>>(q128, k64, v64, do128, a);
+  return launch_status(3);
+}
+
+}  // namespace attnb200
+
+extern "C" {
+
 size_t attn_bwd_workspace_size(const attn_bwd_params_t* p) {
   if (!p) return 0;
-  return 2 * align256((size_t)p->batch * p->num_heads_q * p->seq_q * sizeof(float));
+  const size_t rows = (size_t)p->batch * p->num_heads_q * (bwd_tc_ok(p) ? bwd_seq_pad(p) : p->seq_q);
+  return 2 * align256(rows * sizeof(float));
 }
 
 int attn_bwd(const attn_bwd_params_t* p, void* stream) {
@@ -338,7 +421,8 @@ int attn_bwd(const attn_bwd_params_t* p, void* stream) {
       p->seq_kv <= 0 || p->num_heads_q % p->num_heads_kv != 0)
     return ATTN_ERR_INVALID;
   if (!check_mask(p->mask, p->batch)) return ATTN_ERR_INVALID;
-  if (!simt_dim_ok(p->head_dim)) return ATTN_ERR_UNSUPPORTED;
+  const bool tc = bwd_tc_ok(p);
+  if (!tc && !simt_dim_ok(p->head_dim)) return ATTN_ERR_UNSUPPORTED;
   const size_t need = attn_bwd_workspace_size(p);
   if (!p->workspace || p->workspace_bytes < need) return ATTN_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -358,6 +442,25 @@ int attn_bwd(const attn_bwd_params_t* p, void* stream) {
   a.lse2 = lse2; a.delta = delta;
   a.scale = p->softmax_scale; a.sl2 = p->softmax_scale * kLog2e; a.mask = p->mask;
 
+  if (tc) {
+    int rc;
+    const bool bf = p->dtype == ATTN_BF16;
+    if (p->head_dim == 128)
+      rc = bf ? launch_sm100_bwd<128, true>(p, delta, lse2, st) : launch_sm100_bwd<128, false>(p, delta, lse2, st);
+    else
+      rc = bf ? launch_sm100_bwd<64, true>(p, delta, lse2, st) : launch_sm100_bwd<64, false>(p, delta, lse2, st);
+    if (rc != ATTN_OK || !p->fix_masked_rows) return rc;
+    auto fix = [&](auto tag) {
+      using T = decltype(tag);
+      masked_rows_dv_kernel<T><<<dim3(16, p->num_heads_kv, p->batch), 128, p->head_dim * sizeof(float), st>>>(
+          reinterpret_cast<const T*>(p->d_out), p->do_strides[0], p->do_strides[1], p->do_strides[2],
+          reinterpret_cast<T*>(p->dv), p->dv_strides[0], p->dv_strides[1], p->dv_strides[2], p->lse,
+          p->num_heads_q, p->seq_q, p->seq_kv, p->head_dim, grp);
+    };
+    if (bf) fix(__nv_bfloat16{});
+    else fix(__half{});
+    return launch_status();
+  }
   auto run = [&](auto tag) -> int {
     using T = decltype(tag);
     simt::bwd_prep_kernel<T><<<dim3((p->seq_q + 3) / 4, p->num_heads_q, p->batch), 128, 0, st>>>(
@@ -384,7 +487,7 @@ int attn_bwd(const attn_bwd_params_t* p, void* stream) {
           reinterpret_cast<T*>(p->dv), p->dv_strides[0], p->dv_strides[1], p->dv_strides[2], p->lse,
           p->num_heads_q, p->seq_q, p->seq_kv, p->head_dim, grp);
     }
-    return launch_status();
+    return launch_status(p->fix_masked_rows ? 4 : 3);
   };
   if (p->dtype == ATTN_F32) return run(float{});
   if (p->dtype == ATTN_BF16) return run(__nv_bfloat16{});

@@ -1,0 +1,613 @@
+// Flash-attention backward for sm_100a (tcgen05 + TMA).  The reference has
+// no hand-written backward: its gradients are JAX autodiff of
+// standard_attention (attnax/kernels/attention.py:54-71).  With
+// P = softmax(S), dV = P^T dO, dS = P * (dO V^T - rowsum(dO * O)),
+// dQ = scale * dS K and dK = scale * dS^T Q; P is recomputed from the LSE of
+// the forward.  Two deterministic kernels (no atomics):
+//
+//   dkdv: CTA = 128 kv rows of one (batch, kv head).  Loops over every query
+//         head of the GQA group and every 64-row q tile the mask keeps:
+//           S^T  = K Q^T,  dP^T = V dO^T      (TMEM, double buffered)
+//           dV  += P^T dO, dK  += dS^T Q      (TMEM accumulators)
+//         so dK/dV of a shared KV head are summed over its query heads, the
+//         transpose of the reference's jnp.repeat (attention.py:32-39).
+//   dq:   CTA = 128 q rows of one (batch, query head).  Loops over 64-row kv
+//         tiles:  S = Q K^T, dP = dO V^T, dQ += dS K.
+//
+// Warp roles in both: warps 0-3 own one TMEM lane/row each (elementwise math
+// and epilogue), warp 4 issues TMA, warp 5 allocates TMEM and issues MMAs.
+#include <cfloat>
+
+#include "attn_common.cuh"
+#include "sm100.cuh"
+
+namespace attnb200 {
+namespace bwd {
+
+constexpr int kThreads = 192;
+constexpr int KROWS = 128;  // kv rows per dkdv CTA (MMA M)
+constexpr int QT = 64;      // q rows per dkdv iteration (MMA N)
+constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
+constexpr int KT = 64;      // kv rows per dq iteration (MMA N)
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+struct Args {
+  int B, Hq, Hkv, Sq, Skv, Sq_pad, group;
+  float sl2, scale;
+  const float* lse2;   // [B][Hq][Sq_pad], +inf for padded / fully masked rows
+  const float* delta;  // [B][Hq][Sq_pad]
+  void* dq; void* dk; void* dv;
+  long long dq_s[3], dk_s[3], dv_s[3];
+  attn_mask_t mask;
+};
+
+// q-tile index range [lo, hi) (tiles of QT) that the band allows for kv rows [k0, k1).
+__device__ __forceinline__ void band_q_range(const attn_mask_t& m, int k0, int k1, int Sq, int* lo, int* hi) {
+  const int nq = (Sq + QT - 1) / QT;
+  *lo = 0;
+  *hi = nq;
+  if (m.has_band) {
+    const long long klo = m.kv_offset + k0, khi = m.kv_offset + k1 - 1;
+    long long r_lo = klo + m.band_lo - m.q_offset;  // q - kv >= lo  ->  q >= kv + lo
+    long long r_hi = khi + m.band_hi - m.q_offset;
+    r_lo = ll_max(r_lo, 0);
+    r_hi = ll_min(r_hi, (long long)Sq - 1);
+    if (r_hi < r_lo) {
+      *lo = *hi = 0;
+      return;
+    }
+    *lo = (int)(r_lo / QT);
+    *hi = (int)(r_hi / QT) + 1;
+  }
+}
+
+template <int D>
+struct CfgKV {
+  static constexpr int KCH = D / 64;
+  static constexpr int ST = 2;
+  static constexpr int KV_BYTES = KCH * KROWS * 128;  // K or V tile
+  static constexpr int QD_BYTES = KCH * QT * 128;     // Q or dO tile
+  static constexpr int STAGE = ((2 * QD_BYTES + 2 * QT * 4) + 1023) / 1024 * 1024;  // 1024-aligned
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = KV_BYTES;
+  static constexpr int OFF_ST = 2 * KV_BYTES;                 // stages: Q, dO, lse2, delta
+  static constexpr int OFF_P = OFF_ST + ST * STAGE;           // P^T  [128 kv][64 q] bf16
+  static constexpr int OFF_DS = OFF_P + KROWS * 128;          // dS^T [128 kv][64 q] bf16
+  static constexpr int OFF_BAR = OFF_DS + KROWS * 128;
+  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 2 + 1;
+  static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  // TMEM columns: S^T[2] at 0/64, dP^T[2] at 128/192, dV at 256, dK at 256 + D
+  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 256 + D;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                const __grid_constant__ Args a) {
+  using C = CfgKV<D>;
+  constexpr int ST = C::ST;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t sb = (raw_base + 1023u) & ~1023u;
+  uint8_t* sp = smem_raw + (sb - raw_base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
+  const int k0 = kt * KROWS, k1 = min(k0 + KROWS, a.Skv);
+
+  const uint32_t bar0 = sb + C::OFF_BAR;
+  const uint32_t kv_full = bar0;
+  auto st_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto st_free = [&](int s) { return bar0 + 8u * (1 + ST + s); };
+  auto s_full = [&](int i) { return bar0 + 8u * (1 + 2 * ST + i); };
+  auto s_free = [&](int i) { return bar0 + 8u * (3 + 2 * ST + i); };
+  const uint32_t p_full = bar0 + 8u * (5 + 2 * ST);
+  const uint32_t p_free = bar0 + 8u * (6 + 2 * ST);
+  const uint32_t acc_done = bar0 + 8u * (7 + 2 * ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sp + C::OFF_TMEMPTR);
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(st_full(s), 1);
+      mbar_init(st_free(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(s_free(i), 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(p_free, 1);
+    mbar_init(acc_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int t_lo, t_hi;
+  band_q_range(a.mask, k0, k1, a.Sq, &t_lo, &t_hi);
+  const int ntiles = t_hi - t_lo;
+  const int iters = a.group * ntiles;  // (g, q tile) pairs, g outer
+  auto state_of = [&](int it) {
+    const int qt = t_lo + it % max(ntiles, 1);
+    const int q0 = qt * QT;
+    return tile_state(a.mask, nullptr, nullptr, 0, 0, b, q0, min(q0 + QT, a.Sq), k0, k1, KROWS);
+  };
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      mbar_expect_tx(kv_full, 2 * C::KV_BYTES);
+      for (int c = 0; c < C::KCH; ++c) {
+        tma_load_4d(sb + C::OFF_K + c * KROWS * 128, &tm_k, kv_full, c * 64, k0, hkv, b);
+        tma_load_4d(sb + C::OFF_V + c * KROWS * 128, &tm_v, kv_full, c * 64, k0, hkv, b);
+      }
+      int i = 0;
+      for (int it = 0; it < iters; ++it) {
+        if (state_of(it) == kSkip) continue;
+        const int g = it / ntiles, qt = t_lo + it % ntiles;
+        const int hq = hkv * a.group + g, q0 = qt * QT;
+        const int s = i % ST;
+        if (!mbar_wait(st_free(s), ((i / ST) & 1) ^ 1, kStatusTimeoutLoad)) break;
+        const uint32_t base = sb + C::OFF_ST + s * C::STAGE;
+        mbar_expect_tx(st_full(s), 2 * C::QD_BYTES + 2 * QT * 4);
+        for (int c = 0; c < C::KCH; ++c) {
+          tma_load_4d(base + c * QT * 128, &tm_q, st_full(s), c * 64, q0, hq, b);
+          tma_load_4d(base + C::QD_BYTES + c * QT * 128, &tm_do, st_full(s), c * 64, q0, hq, b);
+        }
+        const long long row = ((long long)b * a.Hq + hq) * a.Sq_pad + q0;
+        bulk_g2s(base + 2 * C::QD_BYTES, a.lse2 + row, QT * 4, st_full(s));
+        bulk_g2s(base + 2 * C::QD_BYTES + QT * 4, a.delta + row, QT * 4, st_full(s));
+        ++i;
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr int FMT = BF16 ? 1 : 0;
+      constexpr uint32_t ID_S = idesc_f16(128, QT, FMT, 0, 0);
+      constexpr uint32_t ID_G = idesc_f16(128, D, FMT, 0, 1);
+      bool ok = mbar_wait(kv_full, 0, kStatusTimeoutMma);
+      auto issue_grads = [&](int j) -> bool {
+        const int s = j % ST;
+        const uint32_t base = sb + C::OFF_ST + s * C::STAGE;
+        if (!mbar_wait(p_full, j & 1, kStatusTimeoutMma)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < QT / 16; ++k) {
+          const uint64_t pa = sdesc_sw128(sb + C::OFF_P + k * 32, 16, 1024);
+          const uint64_t da = sdesc_sw128(sb + C::OFF_DS + k * 32, 16, 1024);
+          const uint64_t dob = sdesc_sw128(base + C::QD_BYTES + k * 16 * 128, QT * 128, 1024);
+          const uint64_t qb = sdesc_sw128(base + k * 16 * 128, QT * 128, 1024);
+          umma_f16(tmem + C::COL_DV, pa, dob, ID_G, (j > 0 || k > 0) ? 1u : 0u);
+          umma_f16(tmem + C::COL_DK, da, qb, ID_G, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(st_free(s));
+        umma_commit(p_free);
+        return true;
+      };
+      int i = 0;
+      for (int it = 0; ok && it < iters; ++it) {
+        if (state_of(it) == kSkip) continue;
+        const int s = i % ST;
+        ok = mbar_wait(st_full(s), (i / ST) & 1, kStatusTimeoutMma) &&
+             mbar_wait(s_free(i & 1), ((i >> 1) & 1) ^ 1, kStatusTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t base = sb + C::OFF_ST + s * C::STAGE;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k & 3) * 32;
+          const uint64_t ka = sdesc_sw128(sb + C::OFF_K + (k >> 2) * KROWS * 128 + off, 16, 1024);
+          const uint64_t va = sdesc_sw128(sb + C::OFF_V + (k >> 2) * KROWS * 128 + off, 16, 1024);
+          const uint64_t qb = sdesc_sw128(base + (k >> 2) * QT * 128 + off, 16, 1024);
+          const uint64_t db = sdesc_sw128(base + C::QD_BYTES + (k >> 2) * QT * 128 + off, 16, 1024);
+          umma_f16(tmem + C::COL_S + (i & 1) * QT, ka, qb, ID_S, k > 0 ? 1u : 0u);
+          umma_f16(tmem + C::COL_DP + (i & 1) * QT, va, db, ID_S, k > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full(i & 1));
+        if (i > 0) ok = issue_grads(i - 1);
+        ++i;
+      }
+      if (ok && i > 0) ok = issue_grads(i - 1);
+      umma_commit(acc_done);
+    }
+  } else {
+    const int r = threadIdx.x;  // kv row within the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    uint8_t* PT = sp + C::OFF_P;
+    uint8_t* DST = sp + C::OFF_DS;
+    int i = 0;
+    bool ok = true;
+    for (int it = 0; it < iters; ++it) {
+      const int st = state_of(it);
+      if (st == kSkip) continue;
+      const int g = it / ntiles, qt = t_lo + it % ntiles;
+      const int hq = hkv * a.group + g, q0 = qt * QT;
+      const int s = i % ST;
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, kStatusTimeoutSoftmax));
+      if (!ok) break;
+      tc_fence_after();
+      float sc[QT], dp[QT];
+#pragma unroll
+      for (int c = 0; c < QT / 32; ++c) {
+        tmem_ld32(tmem + lane_base + C::COL_S + (i & 1) * QT + c * 32,
+                  *reinterpret_cast<uint32_t(*)[32]>(&sc[c * 32]));
+        tmem_ld32(tmem + lane_base + C::COL_DP + (i & 1) * QT + c * 32,
+                  *reinterpret_cast<uint32_t(*)[32]>(&dp[c * 32]));
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(s_free(i & 1));
+      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, k0 + r, q0, min(QT, a.Sq - q0), true);
+      transform_row<QT>(sc, rc, st == kPartial || k0 + r >= a.Skv);
+      const float* sl = reinterpret_cast<const float*>(sp + C::OFF_ST + s * C::STAGE + 2 * C::QD_BYTES);
+      const float* sd = sl + QT;
+      const bool row_ok = k0 + r < a.Skv;
+#pragma unroll
+      for (int c = 0; c < QT; ++c) {
+        const float p = row_ok ? ex2(sc[c] - sl[c]) : 0.f;
+        sc[c] = p;
+        dp[c] = p * (dp[c] - sd[c]);
+      }
+      if (i > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(p_free, (i - 1) & 1, kStatusTimeoutSoftmax));
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int u = 0; u < QT / 8; ++u) {
+        const int c = u * 8;
+        uint4 pv, dv;
+        pv.x = pack2(sc[c], sc[c + 1], BF16); pv.y = pack2(sc[c + 2], sc[c + 3], BF16);
+        pv.z = pack2(sc[c + 4], sc[c + 5], BF16); pv.w = pack2(sc[c + 6], sc[c + 7], BF16);
+        dv.x = pack2(dp[c], dp[c + 1], BF16); dv.y = pack2(dp[c + 2], dp[c + 3], BF16);
+        dv.z = pack2(dp[c + 4], dp[c + 5], BF16); dv.w = pack2(dp[c + 6], dp[c + 7], BF16);
+        const int off = r * 128 + ((u ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(PT + off) = pv;
+        *reinterpret_cast<uint4*>(DST + off) = dv;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      ++i;
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, kStatusTimeoutSoftmax));
+    if (ok) {
+      tc_fence_after();
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      const bool row_ok = k0 + r < a.Skv;
+      T* dvr = reinterpret_cast<T*>(a.dv) + b * a.dv_s[0] + hkv * a.dv_s[1] + (long long)(k0 + r) * a.dv_s[2];
+      T* dkr = reinterpret_cast<T*>(a.dk) + b * a.dk_s[0] + hkv * a.dk_s[1] + (long long)(k0 + r) * a.dk_s[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        T* dst = half ? dkr : dvr;
+        const uint32_t col = half ? C::COL_DK : C::COL_DV;
+        const float mul = half ? a.scale : 1.f;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          if (i > 0) {
+            tmem_ld32(tmem + lane_base + col + c * 32, o);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack2(__uint_as_float(o[v * 8 + 0]) * mul, __uint_as_float(o[v * 8 + 1]) * mul, BF16);
+              w.y = pack2(__uint_as_float(o[v * 8 + 2]) * mul, __uint_as_float(o[v * 8 + 3]) * mul, BF16);
+              w.z = pack2(__uint_as_float(o[v * 8 + 4]) * mul, __uint_as_float(o[v * 8 + 5]) * mul, BF16);
+              w.w = pack2(__uint_as_float(o[v * 8 + 6]) * mul, __uint_as_float(o[v * 8 + 7]) * mul, BF16);
+              *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------- dQ ----
+template <int D>
+struct CfgQ {
+  static constexpr int KCH = D / 64;
+  static constexpr int ST = 3;
+  static constexpr int Q_BYTES = KCH * QROWS * 128;   // Q or dO
+  static constexpr int KV_BYTES = KCH * KT * 128;     // K or V tile
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = Q_BYTES;
+  static constexpr int OFF_ST = 2 * Q_BYTES;          // stages: K, V
+  static constexpr int OFF_DS = OFF_ST + ST * 2 * KV_BYTES;  // dS [128 q][64 kv] bf16
+  static constexpr int OFF_BAR = OFF_DS + QROWS * 128;
+  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 2 + 1;
+  static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  // S[2] at 0/64, dP[2] at 128/192, dQ at 256
+  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DQ = 256;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+              const __grid_constant__ Args a) {
+  using C = CfgQ<D>;
+  constexpr int ST = C::ST;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t sb = (raw_base + 1023u) & ~1023u;
+  uint8_t* sp = smem_raw + (sb - raw_base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqt = (a.Sq + QROWS - 1) / QROWS;
+  const int qt = nqt - 1 - (int)blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
+  const int hkv = hq / a.group;
+  const int q0 = qt * QROWS, q1 = min(q0 + QROWS, a.Sq);
+
+  const uint32_t bar0 = sb + C::OFF_BAR;
+  const uint32_t q_full = bar0;
+  auto st_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto st_free = [&](int s) { return bar0 + 8u * (1 + ST + s); };
+  auto s_full = [&](int i) { return bar0 + 8u * (1 + 2 * ST + i); };
+  auto s_free = [&](int i) { return bar0 + 8u * (3 + 2 * ST + i); };
+  const uint32_t ds_full = bar0 + 8u * (5 + 2 * ST);
+  const uint32_t ds_free = bar0 + 8u * (6 + 2 * ST);
+  const uint32_t acc_done = bar0 + 8u * (7 + 2 * ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sp + C::OFF_TMEMPTR);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(st_full(s), 1);
+      mbar_init(st_free(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(s_free(i), 128);
+    }
+    mbar_init(ds_full, 128);
+    mbar_init(ds_free, 1);
+    mbar_init(acc_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int j_lo, j_hi;
+  band_tile_range(a.mask, q0, q1, a.Skv, KT, &j_lo, &j_hi);
+  auto state_of = [&](int j) {
+    return tile_state(a.mask, nullptr, nullptr, 0, 0, b, q0, q1, j * KT, min((j + 1) * KT, a.Skv), KT);
+  };
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      mbar_expect_tx(q_full, 2 * C::Q_BYTES);
+      for (int c = 0; c < C::KCH; ++c) {
+        tma_load_4d(sb + C::OFF_Q + c * QROWS * 128, &tm_q, q_full, c * 64, q0, hq, b);
+        tma_load_4d(sb + C::OFF_DO + c * QROWS * 128, &tm_do, q_full, c * 64, q0, hq, b);
+      }
+      int i = 0;
+      for (int j = j_lo; j < j_hi; ++j) {
+        if (state_of(j) == kSkip) continue;
+        const int s = i % ST;
+        if (!mbar_wait(st_free(s), ((i / ST) & 1) ^ 1, kStatusTimeoutLoad)) break;
+        const uint32_t base = sb + C::OFF_ST + s * 2 * C::KV_BYTES;
+        mbar_expect_tx(st_full(s), 2 * C::KV_BYTES);
+        for (int c = 0; c < C::KCH; ++c) {
+          tma_load_4d(base + c * KT * 128, &tm_k, st_full(s), c * 64, j * KT, hkv, b);
+          tma_load_4d(base + C::KV_BYTES + c * KT * 128, &tm_v, st_full(s), c * 64, j * KT, hkv, b);
+        }
+        ++i;
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr int FMT = BF16 ? 1 : 0;
+      constexpr uint32_t ID_S = idesc_f16(128, KT, FMT, 0, 0);
+      constexpr uint32_t ID_Q = idesc_f16(128, D, FMT, 0, 1);
+      bool ok = mbar_wait(q_full, 0, kStatusTimeoutMma);
+      auto issue_dq = [&](int j) -> bool {
+        const int s = j % ST;
+        const uint32_t base = sb + C::OFF_ST + s * 2 * C::KV_BYTES;
+        if (!mbar_wait(ds_full, j & 1, kStatusTimeoutMma)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < KT / 16; ++k) {
+          const uint64_t da = sdesc_sw128(sb + C::OFF_DS + k * 32, 16, 1024);
+          const uint64_t kb = sdesc_sw128(base + k * 16 * 128, KT * 128, 1024);
+          umma_f16(tmem + C::COL_DQ, da, kb, ID_Q, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(st_free(s));
+        umma_commit(ds_free);
+        return true;
+      };
+      int i = 0;
+      for (int j = j_lo; ok && j < j_hi; ++j) {
+        if (state_of(j) == kSkip) continue;
+        const int s = i % ST;
+        ok = mbar_wait(st_full(s), (i / ST) & 1, kStatusTimeoutMma) &&
+             mbar_wait(s_free(i & 1), ((i >> 1) & 1) ^ 1, kStatusTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t base = sb + C::OFF_ST + s * 2 * C::KV_BYTES;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k & 3) * 32;
+          const uint64_t qa = sdesc_sw128(sb + C::OFF_Q + (k >> 2) * QROWS * 128 + off, 16, 1024);
+          const uint64_t oa = sdesc_sw128(sb + C::OFF_DO + (k >> 2) * QROWS * 128 + off, 16, 1024);
+          const uint64_t kb = sdesc_sw128(base + (k >> 2) * KT * 128 + off, 16, 1024);
+          const uint64_t vb = sdesc_sw128(base + C::KV_BYTES + (k >> 2) * KT * 128 + off, 16, 1024);
+          umma_f16(tmem + C::COL_S + (i & 1) * KT, qa, kb, ID_S, k > 0 ? 1u : 0u);
+          umma_f16(tmem + C::COL_DP + (i & 1) * KT, oa, vb, ID_S, k > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full(i & 1));
+        if (i > 0) ok = issue_dq(i - 1);
+        ++i;
+      }
+      if (ok && i > 0) ok = issue_dq(i - 1);
+      umma_commit(acc_done);
+    }
+  } else {
+    const int r = threadIdx.x;  // q row within the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const bool row_ok = q0 + r < a.Sq;
+    const long long ridx = ((long long)b * a.Hq + hq) * a.Sq_pad + q0 + r;
+    const float lse2 = a.lse2[ridx], delta = a.delta[ridx];
+    uint8_t* DS = sp + C::OFF_DS;
+    int i = 0;
+    bool ok = true;
+    for (int j = j_lo; j < j_hi; ++j) {
+      const int st = state_of(j);
+      if (st == kSkip) continue;
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, kStatusTimeoutSoftmax));
+      if (!ok) break;
+      tc_fence_after();
+      float sc[KT], dp[KT];
+#pragma unroll
+      for (int c = 0; c < KT / 32; ++c) {
+        tmem_ld32(tmem + lane_base + C::COL_S + (i & 1) * KT + c * 32,
+                  *reinterpret_cast<uint32_t(*)[32]>(&sc[c * 32]));
+        tmem_ld32(tmem + lane_base + C::COL_DP + (i & 1) * KT + c * 32,
+                  *reinterpret_cast<uint32_t(*)[32]>(&dp[c * 32]));
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(s_free(i & 1));
+      const int k0 = j * KT;
+      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, k0, min(KT, a.Skv - k0), false);
+      transform_row<KT>(sc, rc, st == kPartial);
+#pragma unroll
+      for (int c = 0; c < KT; ++c) {
+        const float p = ex2(sc[c] - lse2);
+        dp[c] = p * (dp[c] - delta);
+      }
+      if (i > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(ds_free, (i - 1) & 1, kStatusTimeoutSoftmax));
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int u = 0; u < KT / 8; ++u) {
+        const int c = u * 8;
+        uint4 w;
+        w.x = pack2(dp[c], dp[c + 1], BF16); w.y = pack2(dp[c + 2], dp[c + 3], BF16);
+        w.z = pack2(dp[c + 4], dp[c + 5], BF16); w.w = pack2(dp[c + 6], dp[c + 7], BF16);
+        *reinterpret_cast<uint4*>(DS + r * 128 + ((u ^ (r & 7)) << 4)) = w;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+      ++i;
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, kStatusTimeoutSoftmax));
+    if (ok) {
+      tc_fence_after();
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* dqr = reinterpret_cast<T*>(a.dq) + b * a.dq_s[0] + hq * a.dq_s[1] + (long long)(q0 + r) * a.dq_s[2];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (i > 0) {
+          tmem_ld32(tmem + lane_base + C::COL_DQ + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack2(__uint_as_float(o[v * 8 + 0]) * a.scale, __uint_as_float(o[v * 8 + 1]) * a.scale, BF16);
+            w.y = pack2(__uint_as_float(o[v * 8 + 2]) * a.scale, __uint_as_float(o[v * 8 + 3]) * a.scale, BF16);
+            w.z = pack2(__uint_as_float(o[v * 8 + 4]) * a.scale, __uint_as_float(o[v * 8 + 5]) * a.scale, BF16);
+            w.w = pack2(__uint_as_float(o[v * 8 + 6]) * a.scale, __uint_as_float(o[v * 8 + 7]) * a.scale, BF16);
+            *reinterpret_cast<uint4*>(dqr + c * 32 + v * 8) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// delta = rowsum(dO * O), lse2 = lse * log2(e) into [B][H][S_pad] with
+// padded rows (+inf, 0) so bulk copies of whole 64-row tiles stay in bounds.
+template <typename T>
+__global__ void prep_pad_kernel(const T* out, const T* dout, long long os0, long long os1, long long os2,
+                                long long ds0, long long ds1, long long ds2, const float* lse,
+                                float* delta, float* lse2, int H, int S, int S_pad, int D) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  if (row >= S_pad) return;
+  const long long idx = ((long long)b * H + h) * S_pad + row;
+  if (row >= S) {
+    if (lane == 0) {
+      delta[idx] = 0.f;
+      lse2[idx] = INFINITY;
+    }
+    return;
+  }
+  const T* o = out + b * os0 + h * os1 + (long long)row * os2;
+  const T* d = dout + b * ds0 + h * ds1 + (long long)row * ds2;
+  float acc = 0.f;
+  for (int e = lane * 8; e < D; e += 256) {
+    const uint4 ov = *reinterpret_cast<const uint4*>(o + e);
+    const uint4 dv = *reinterpret_cast<const uint4*>(d + e);
+    const T* oh = reinterpret_cast<const T*>(&ov);
+    const T* dh = reinterpret_cast<const T*>(&dv);
+#pragma unroll
+    for (int x = 0; x < 8; ++x) acc = fmaf(to_f32(oh[x]), to_f32(dh[x]), acc);
+  }
+  for (int x = 16; x > 0; x >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, x);
+  if (lane == 0) {
+    delta[idx] = acc;
+    const float l = lse[((long long)b * H + h) * S + row];
+    lse2[idx] = (l == -INFINITY) ? INFINITY : l * kLog2e;
+  }
+}
+
+}  // namespace bwd
+}  // namespace attnb200

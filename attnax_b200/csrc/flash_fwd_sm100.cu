@@ -189,8 +189,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------- softmax --
     const int r = threadIdx.x;  // query row within the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const float slope_l2 = a.mask.alibi_slopes ? a.mask.alibi_slopes[hq] * kLog2e : 0.f;
-    const bool simple = (a.mask.alibi_slopes == nullptr);
     float m_run = -FLT_MAX, l_run = 0.f;
     int i = 0;
     bool ok = true;
@@ -210,21 +208,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(s_free(i & 1));
 
+      const int k0 = j * BN;
+      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, k0, min(BN, a.Skv - k0), false);
+      transform_row<BN>(s, rc, st == kPartial);
       float mx = m_run;
-      if (st == kFull && simple) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          s[c] *= a.sl2;
-          mx = fmaxf(mx, s[c]);
-        }
-      } else {
-        const int k0 = j * BN;
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          s[c] = mask_score(a.mask, s[c], a.sl2, slope_l2, b, hq, q0 + r, k0 + c, a.Skv, st == kPartial);
-          mx = fmaxf(mx, s[c]);
-        }
-      }
+      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
       const float alpha = ex2(m_run - mx);
       float sum = 0.f;
 #pragma unroll
@@ -235,23 +224,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       l_run = l_run * alpha + sum;
       m_run = mx;
 
+      // PV of the previous tile must be done before P is overwritten and O rescaled.
       if (i > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (i - 1) & 1, kStatusTimeoutSoftmax));
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            const uint32_t ta = tmem + lane_base + C::O_COL + c * 32;
-            tmem_ld32(ta, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(ta, o);
-          }
-          tmem_wait_st();
-        }
       }
       // P (bf16/f16) into the K-major 128B-swizzled tile the PV MMA reads.
 #pragma unroll
@@ -264,6 +241,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         val.w = pack2(s[c + 6], s[c + 7], BF16);
         const int chunk = c >> 6, unit = (c & 63) >> 3;
         *reinterpret_cast<uint4*>(P + chunk * BM * 128 + r * 128 + ((unit ^ (r & 7)) << 4)) = val;
+      }
+      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          const uint32_t ta = tmem + lane_base + C::O_COL + c * 32;
+          tmem_ld32(ta, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(ta, o);
+        }
+        tmem_wait_st();
       }
       fence_proxy_async_smem();
       tc_fence_before();

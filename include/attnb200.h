@@ -164,6 +164,8 @@ int attn_ring_fwd(const attn_ring_params_t* p, void* comm, void* compute_stream,
 int attn_device_status(int32_t* status);
 const char* attn_status_string(int status);
 int attn_version(void);
+/* Number of kernels this library has launched in this process. */
+uint64_t attn_launch_count(void);
 
 #ifdef __cplusplus
 }
