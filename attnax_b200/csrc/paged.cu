@@ -327,7 +327,8 @@ __global__ void paged_combine_kernel(const float* part_o, const float* part_lse,
   const int ctx = seq_lens[seq];
   const long long prow = (long long)seq * Hq * Sq + row;
   T* orow = out + prow * D;
-  const int n = (ctx + chunk_tokens - 1) / chunk_tokens;
+  // max_context bounds the lengths by contract; clamp so a violation cannot read past the partials.
+  const int n = min((ctx + chunk_tokens - 1) / chunk_tokens, max_splits);
   if (n == 0) {  // empty sequence: zeros (paged.py:53-54)
     for (int d = threadIdx.x; d < D; d += blockDim.x) orow[d] = from_f32<T>(0.f);
     return;
