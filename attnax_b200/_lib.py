@@ -86,6 +86,7 @@ SIGNATURES = {
     "attn_bwd": (C.c_int, [C.POINTER(BwdParams), vp]),
     "attn_paged_decode_workspace_size": (szt, [C.POINTER(PagedParams)]),
     "attn_paged_decode": (C.c_int, [C.POINTER(PagedParams), vp]),
+    "attn_paged_decode_static": (C.c_int, [C.POINTER(PagedParams), vp]),
     "attn_paged_gather": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, vp, i32, vp, vp, vp]),
     "attn_paged_append": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, vp, i32, i32, vp, vp, vp, vp]),
     "attn_comm_unique_id": (C.c_int, [vp, szt]),

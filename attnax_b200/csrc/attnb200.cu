@@ -729,3 +729,5 @@ int attn_ring_fwd(const attn_ring_params_t* p, void* comm, void* compute_stream,
 }
 
 }  // extern "C"
+
+#include "paged_static.cu"

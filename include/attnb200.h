@@ -137,6 +137,20 @@ int attn_bwd(const attn_bwd_params_t* p, void* stream);
 /* ---- paged KV cache ----------------------------------------------------- */
 size_t attn_paged_decode_workspace_size(const attn_paged_params_t* p);
 int attn_paged_decode(const attn_paged_params_t* p, void* stream);
+/* Allocation-free paged decode.  No counterpart in the reference.  Same
+ * inputs, outputs and results as attn_paged_decode, but its split partials
+ * live in an 8 MiB array inside the library (one per GPU that loads it,
+ * held until exit), so it works for callers that must not allocate device
+ * memory: code running while a CUDA graph is being captured, serving loops
+ * whose allocator forbids cudaMalloc on the hot path (it synchronises the
+ * device), and embedders with a fixed memory budget.  `workspace` is
+ * ignored.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream
+ * capture.  The split count shrinks to fit the array; requests whose
+ * num_seqs * num_heads_q * seq_q * (head_dim + 1) floats exceed 8 MiB are
+ * rejected with ATTN_ERR_WORKSPACE.  All calls share the array: calls that
+ * overlap on the GPU (different streams, no ordering) race. */
+int attn_paged_decode_static(const attn_paged_params_t* p, void* stream);
 /* Contiguous copy of sequence `seq`: keys/values [seq_len, heads_kv, head_dim]. */
 int attn_paged_gather(attn_dtype_t dtype, const void* key_pool, const void* value_pool,
                       int32_t block_size, int32_t heads_kv, int32_t head_dim,
