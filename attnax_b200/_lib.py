@@ -68,16 +68,6 @@ class PagedParams(C.Structure):
     ]
 
 
-class RingParams(C.Structure):
-    _fields_ = [
-        ("dtype", C.c_int), ("batch", i32), ("num_heads_q", i32), ("num_heads_kv", i32),
-        ("seq_local", i32), ("head_dim", i32),
-        ("q", vp), ("k", vp), ("v", vp), ("out", vp), ("lse", vp),
-        ("softmax_scale", f32), ("causal", i32), ("balance", i32),
-        ("workspace", vp), ("workspace_bytes", szt),
-    ]
-
-
 # Every symbol the header declares, with its ctypes signature.
 SIGNATURES = {
     "attn_fwd_workspace_size": (szt, [C.POINTER(FwdParams)]),
@@ -89,11 +79,7 @@ SIGNATURES = {
     "attn_paged_decode_static": (C.c_int, [C.POINTER(PagedParams), vp]),
     "attn_paged_gather": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, vp, i32, vp, vp, vp]),
     "attn_paged_append": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, vp, i32, i32, vp, vp, vp, vp]),
-    "attn_comm_unique_id": (C.c_int, [vp, szt]),
-    "attn_comm_init": (C.c_int, [vp, i32, i32, C.POINTER(vp)]),
-    "attn_comm_destroy": (C.c_int, [vp]),
-    "attn_ring_workspace_size": (szt, [C.POINTER(RingParams), i32]),
-    "attn_ring_fwd": (C.c_int, [C.POINTER(RingParams), vp, vp, vp]),
+    "attn_lse_merge": (C.c_int, [C.c_int, i64, i32, vp, vp, vp, vp, vp, vp]),
     "attn_device_status": (C.c_int, [C.POINTER(i32)]),
     "attn_status_string": (C.c_char_p, [C.c_int]),
     "attn_version": (C.c_int, []),

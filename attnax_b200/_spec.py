@@ -16,7 +16,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib
-from ._api import ComposedScoreMod, mask_mod_to_boolean_mask
+from ._api import ComposedScoreMod, position_indices
 from .score_mods import (AdditiveBiasMod, AlibiMod, CausalMod, DocumentMaskMod, MaskModScoreMod,
                          PrefixLMMod, SlidingWindowMod)
 
@@ -90,8 +90,9 @@ def build_spec(score_mod, mask, *, batch, heads_q, seq_q, seq_kv, device, q_offs
             b = p.bias.to(device)
             bias = b if bias is None else bias + b
         elif isinstance(p, MaskModScoreMod):
-            bm = mask_mod_to_boolean_mask(p.mask_mod, batch=batch, num_heads=heads_q, seq_q=seq_q,
-                                          seq_kv=seq_kv, device=device)
+            # MaskMods see global positions (attention.py:651-657), like every other mod.
+            idx = position_indices(batch, heads_q, seq_q, seq_kv, device, q_offset, kv_offset)
+            bm = torch.as_tensor(p.mask_mod(*idx)).expand(batch, heads_q, seq_q, seq_kv)
             bmask = bm if bmask is None else (bmask & bm)
         else:
             raise NotImplementedError(
@@ -143,3 +144,25 @@ def build_spec(score_mod, mask, *, batch, heads_q, seq_q, seq_kv, device, q_offs
     diag_kept = (q_offset == kv_offset and seq_q <= seq_kv and lo <= 0 <= hi)
     fix = bmask is not None or (has_sel and not diag_kept)
     return MaskSpec(m, keep, fix, has_sel)
+
+
+def band_of(score_mod):
+    """(lo, hi) of the causal/window selection of a mod chain, or None."""
+    lo, hi, has = -BAND_INF, BAND_INF, False
+    for p in flatten_mods(score_mod):
+        if isinstance(p, CausalMod):
+            lo, has = max(lo, 0), True
+        elif isinstance(p, SlidingWindowMod):
+            lo = max(lo, 0 if p.causal else -(p.window_size - 1))
+            hi = min(hi, p.window_size - 1)
+            has = True
+    return (lo, hi) if has else None
+
+
+def may_empty_rows(score_mod, mask) -> bool:
+    """Whether some query row could keep no key at all (needs the mean-of-V rule)."""
+    for p in flatten_mods(score_mod):
+        if isinstance(p, (MaskModScoreMod, DocumentMaskMod, PrefixLMMod)):
+            return True
+    band = band_of(score_mod)
+    return mask is not None or (band is not None and not (band[0] <= 0 <= band[1]))

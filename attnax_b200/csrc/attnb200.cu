@@ -686,48 +686,26 @@ int attn_paged_decode(const attn_paged_params_t* p, void* stream) {
   return bf ? launch_paged<8, true>(p, w, ws, st) : launch_paged<8, false>(p, w, ws, st);
 }
 
-int attn_comm_unique_id(void* out, size_t out_bytes) {
-  if (!out || out_bytes < sizeof(ncclUniqueId)) return ATTN_ERR_INVALID;
-  ncclUniqueId id;
-  if (ncclGetUniqueId(&id) != ncclSuccess) return ATTN_ERR_NCCL;
-  memcpy(out, &id, sizeof(id));
-  return ATTN_OK;
-}
-
-int attn_comm_init(const void* unique_id, int32_t nranks, int32_t rank, void** comm) {
-  if (!unique_id || !comm || nranks <= 0 || rank < 0 || rank >= nranks) return ATTN_ERR_INVALID;
-  ncclUniqueId id;
-  memcpy(&id, unique_id, sizeof(id));
-  auto* c = new ring::Comm;
-  c->nranks = nranks;
-  c->rank = rank;
-  if (ncclCommInitRank(&c->comm, nranks, id, rank) != ncclSuccess) {
-    delete c;
-    return ATTN_ERR_NCCL;
-  }
-  *comm = c;
-  return ATTN_OK;
-}
-
-int attn_comm_destroy(void* comm) {
-  auto* c = reinterpret_cast<ring::Comm*>(comm);
-  if (!c) return ATTN_ERR_INVALID;
-  const ncclResult_t r = c->comm ? ncclCommDestroy(c->comm) : ncclSuccess;
-  delete c;
-  return r == ncclSuccess ? ATTN_OK : ATTN_ERR_NCCL;
-}
-
-size_t attn_ring_workspace_size(const attn_ring_params_t* p, int32_t nranks) {
-  (void)p;
-  (void)nranks;
-  return 0;
-}
-
-int attn_ring_fwd(const attn_ring_params_t* p, void* comm, void* compute_stream, void* comm_stream) {
-  (void)p; (void)comm; (void)compute_stream; (void)comm_stream;
-  return ATTN_ERR_UNSUPPORTED;
-}
-
 }  // extern "C"
 
 #include "paged_static.cu"
+
+extern "C" int attn_lse_merge(attn_dtype_t dtype, int64_t rows, int32_t head_dim, float* o_acc,
+                              float* lse_acc, const void* o_part, const float* lse_part, void* out,
+                              void* stream) {
+  using namespace attnb200;
+  if (rows < 0 || head_dim <= 0 || !o_acc || !lse_acc || !o_part || !lse_part) return ATTN_ERR_INVALID;
+  if (rows == 0) return ATTN_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+#define ATTN_MERGE(T)                                                                         \
+  ring::lse_merge_kernel<T><<<grid, 256, 0, st>>>(rows, head_dim, o_acc, lse_acc,             \
+                                                  reinterpret_cast<const T*>(o_part), lse_part, \
+                                                  reinterpret_cast<T*>(out))
+  if (dtype == ATTN_F32) ATTN_MERGE(float);
+  else if (dtype == ATTN_BF16) ATTN_MERGE(__nv_bfloat16);
+  else if (dtype == ATTN_F16) ATTN_MERGE(__half);
+  else return ATTN_ERR_INVALID;
+#undef ATTN_MERGE
+  return launch_status();
+}

@@ -9,7 +9,7 @@ names fall back to the local flash kernel the same way.
 
 from __future__ import annotations
 
-from .flash import attention, _output_dropout
+from .flash import _output_dropout, attention
 
 _AXES = {}
 
@@ -34,10 +34,71 @@ def ring_attention(query, key, value, *, mask=None, score_mod=None, dropout_rng=
     if axis_name is None or axis_name not in _AXES:
         out = attention(query, key, value, mask=mask, score_mod=score_mod)
         return _output_dropout(out, dropout_rng, dropout_rate, deterministic)
-    from ._ring_impl import ring_forward
-
     out = ring_forward(query, key, value, mask=mask, score_mod=score_mod, group=_AXES[axis_name])
     return _output_dropout(out, dropout_rng, dropout_rate, deterministic)
+
+
+def ring_forward(query, key, value, *, mask=None, score_mod=None, group=None, zigzag=None):
+    """Ring attention of the local shards over every rank of ``group``.
+
+    ``query`` (B, Hq, S, D) and ``key``/``value`` (B, Hkv, S, D) are this
+    rank's contiguous shard of the global sequence; returns this rank's
+    output shard.  ``mask`` (and an additive bias) are local
+    ``(.., S, S)`` tensors applied at every step, as in the reference
+    (attention.py:659-660).  Forward only.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from ._ring_impl import KernelOps, RingSchedule, ring_schedule_forward
+    from ._spec import band_of, may_empty_rows
+    from .flash import check_qkv
+
+    B, Hq, Hkv, S, Skv, D = check_qkv(query, key, value)
+    if S != Skv:
+        raise ValueError("ring_attention needs equal local query and key/value shard lengths")
+    if torch.is_grad_enabled() and (query.requires_grad or key.requires_grad or value.requires_grad):
+        raise NotImplementedError("ring_attention backward is not implemented; call it under no_grad")
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    band = band_of(score_mod)
+    if zigzag is None:
+        zigzag = band is not None and band[0] >= 0 and world > 1
+    sched = RingSchedule(world, rank, S, zigzag)
+    ops = KernelOps(group, score_mod, mask, B, Hq, S, query.device)
+    out, acc = ring_schedule_forward(query.contiguous(), key.contiguous(), value.contiguous(),
+                                     ops=ops, sched=sched, band=band)
+    if may_empty_rows(score_mod, mask):
+        out = _fill_empty_rows(out, sched, acc, value, group)
+    return out
+
+
+def _fill_empty_rows(out, sched, acc, value, group):
+    """Rows that kept no key anywhere average the whole global V (the reference's softmax of
+    an all-finfo.min row); every rank joins the all-reduce so the collective order matches."""
+    import torch
+    import torch.distributed as dist
+
+    from ._ring_impl import redeal
+
+    vsum = value.float().sum(dim=2)                      # (B, Hkv, D)
+    dist.all_reduce(vsum, group=group)
+    n_glob = value.shape[2] * dist.get_world_size(group)
+    lse = torch.cat([a[1] for a in acc], dim=2)[..., None]  # (B, Hq, S, 1) in ring layout
+    if sched.zigzag:
+        (lse,) = redeal(sched, _Xchg(group), [lse], to_work=False)
+    grp = out.shape[1] // value.shape[1]
+    mean = (vsum / n_glob).repeat_interleave(grp, dim=1)[:, :, None, :].to(out.dtype)
+    return torch.where(lse == float("-inf"), mean, out)
+
+
+class _Xchg:
+    def __init__(self, group):
+        from ._ring_impl import DistExchange
+
+        self._x = DistExchange(group)
+
+    def exchange(self, sends, recvs):
+        self._x.exchange(sends, recvs)
 
 
 def ring_attention_reference(query, key, value, *, mask=None, score_mod=None):

@@ -356,6 +356,41 @@ def run_document(args, torch, peaks):
                          "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4)}}
 
 
+def run_ring(args, torch, dist, rank, world, peaks):
+    """Ring attention, B1 Hq32 Hkv8 D128 causal, global S split over the ranks (strong scaling)."""
+    import attnax_b200 as ax
+    from attnax_b200.ring import ring_forward
+
+    S = 131072 if args.scale == "full" else 16384
+    Hq, Hkv, D = 32, 8, 128
+    Sl = S // world
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    q = torch.randn(1, Hq, Sl, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, Hkv, Sl, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, Hkv, Sl, D, generator=g, device=dev).to(torch.bfloat16)
+    mod = ax.causal_mod()
+    grp = dist.group.WORLD if world > 1 else None
+    tm = Timer(torch, dist, world)
+
+    def step(marks):
+        with torch.no_grad():
+            if world > 1:
+                ring_forward(q, k, v, score_mod=mod, group=grp)
+            else:
+                ax.flash_attention(q, k, v, score_mod=mod)
+
+    steps = max(2, min(args.steps, 5))
+    ms, _ = tm.run(step, steps, 3)
+    fl = 4.0 * D * Hq * S * (S + 1) / 2
+    tf = fl / (ms * 1e-3) / 1e12
+    return {"metric": "ring attention tokens/s", "value": round(S / (ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": world, "ms_per_step": round(ms, 3), "tflops_total": round(tf, 2),
+            "tflops_per_gpu": round(tf / world, 2), "scaling": "strong",
+            "config": f"B1 S{S} (S/P={Sl}) Hq{Hq} Hkv{Hkv} D{D} bf16 causal, "
+                      f"{'zig-zag ring over NCCL' if world > 1 else 'one GPU, flash kernel'}"}
+
+
 def run_fp32(args, torch, peaks):
     import attnax_b200 as ax
     from attnax_b200._spec import build_spec
@@ -435,7 +470,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["flash", "paged", "document", "fp32"], default="flash")
+    ap.add_argument("--workload", choices=["flash", "paged", "document", "fp32", "ring"], default="flash")
     ap.add_argument("--scale", choices=["full", "small"], default="full")
     ap.add_argument("--no-secondary", action="store_true")
     args = ap.parse_args()
@@ -483,8 +518,9 @@ def main():
                 v, dt, sample = run_cpu_flash("baseline")
                 line["cpu_baseline"] = {"value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(),
                                         "kind": "port", "sample": sample, "seconds": round(dt, 2)}
+            ring = None if args.no_secondary else run_ring(args, torch, dist, rank, world, peaks)
             if rank == 0 and not args.no_secondary:
-                line["secondary"] = {"paged": run_paged(args, torch, peaks),
+                line["secondary"] = {"ring": ring, "paged": run_paged(args, torch, peaks),
                                      "document": run_document(args, torch, peaks),
                                      "fp32": run_fp32(args, torch, peaks)}
             if world > 1:
@@ -493,6 +529,8 @@ def main():
             line = run_paged(args, torch, peaks)
         elif args.workload == "document":
             line = run_document(args, torch, peaks)
+        elif args.workload == "ring":
+            line = run_ring(args, torch, dist, rank, world, peaks)
         else:
             line = run_fp32(args, torch, peaks)
         if rank == 0:

@@ -20,10 +20,10 @@
  *                       PagedKVCache block tables (attnax/paged_cache.py:12-48)
  *   attn_paged_gather   gather_kv (attnax/paged_cache.py:201-231)
  *   attn_paged_append   append_kv (attnax/paged_cache.py:144-198)
- *   attn_ring_fwd       ring_attention (attnax/kernels/attention.py:540-691),
- *                       the lax.ppermute ring (:673-674) done with NCCL
- *   attn_comm_*         the device-axis binding that jax.lax.axis_index /
- *                       axis_size (:604-617) provide in the reference
+ *   attn_lse_merge      the per-step softmax merge of ring_attention
+ *                       (attnax/kernels/attention.py:662-671); the K/V
+ *                       rotation (:673-674) is NCCL send/recv on the caller's
+ *                       process group
  */
 #ifndef ATTNB200_H_
 #define ATTNB200_H_
@@ -117,17 +117,6 @@ typedef struct {
   void* workspace; size_t workspace_bytes;
 } attn_paged_params_t;
 
-typedef struct {
-  attn_dtype_t dtype;
-  int32_t batch, num_heads_q, num_heads_kv, seq_local, head_dim;
-  const void* q; const void* k; const void* v; void* out;   /* contiguous local shards */
-  float* lse;                    /* [batch, heads_q, seq_local] or NULL */
-  float softmax_scale;
-  int32_t causal;                /* causal_mod with global positions */
-  int32_t balance;               /* 1: zig-zag re-sharding for causal load balance */
-  void* workspace; size_t workspace_bytes;
-} attn_ring_params_t;
-
 /* ---- flash attention ---------------------------------------------------- */
 size_t attn_fwd_workspace_size(const attn_fwd_params_t* p);
 int attn_fwd(const attn_fwd_params_t* p, void* stream);
@@ -164,13 +153,17 @@ int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool,
                       const void* keys_new, const void* values_new,
                       int32_t* bad_slot, void* stream);
 
-/* ---- ring attention over NCCL -------------------------------------------- */
-int attn_comm_unique_id(void* out, size_t out_bytes);       /* 128 bytes */
-int attn_comm_init(const void* unique_id, int32_t nranks, int32_t rank, void** comm);
-int attn_comm_destroy(void* comm);
-size_t attn_ring_workspace_size(const attn_ring_params_t* p, int32_t nranks);
-int attn_ring_fwd(const attn_ring_params_t* p, void* comm, void* compute_stream,
-                  void* comm_stream);
+/* ---- ring attention ------------------------------------------------------ */
+/* Merges one partial attention result into a running one, row by row, by
+ * log-sum-exp (the per-step online-softmax update of ring_attention,
+ * attnax/kernels/attention.py:662-671, done once per K/V block):
+ *   m = max(lse_acc, lse_part); w_a = e^(lse_acc - m); w_p = e^(lse_part - m)
+ *   o_acc = (w_a o_acc + w_p o_part) / (w_a + w_p); lse_acc = m + log(w_a + w_p)
+ * Rows with lse_part = -inf (no kept key) leave the running result unchanged.
+ * o_acc is float32 [rows, head_dim]; o_part has `dtype`; with `out` non-NULL
+ * the merged rows are also written there in `dtype` (the final step). */
+int attn_lse_merge(attn_dtype_t dtype, int64_t rows, int32_t head_dim, float* o_acc, float* lse_acc,
+                   const void* o_part, const float* lse_part, void* out, void* stream);
 
 /* ---- diagnostics -------------------------------------------------------- */
 /* Reads and clears the device status word that bounded waits set on

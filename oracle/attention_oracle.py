@@ -290,9 +290,13 @@ def standard_attention(query, key, value, *, mask=None, score_mod=None):
     return np.einsum("bhqk,bhkd->bhqd", p, value).astype(query.dtype)
 
 
-def standard_attention_lse(query, key, value, *, mask=None, score_mod=None):
-    """``standard_attention`` plus the natural-log LSE of each score row."""
-    s = _final_scores(query, key, mask, score_mod)
+def standard_attention_lse(query, key, value, *, mask=None, score_mod=None, q_offset=0, kv_offset=0):
+    """``standard_attention`` plus the natural-log LSE of each score row.
+
+    ``q_offset``/``kv_offset`` are the global positions of row/column 0 given
+    to ``score_mod`` (one ring step, attention.py:641-657).
+    """
+    s = _final_scores(query, key, mask, score_mod, q_offset, kv_offset)
     m = np.max(s, axis=-1, keepdims=True)
     e = np.exp(s - m)
     l = np.sum(e, axis=-1, keepdims=True)

@@ -20,7 +20,7 @@ def header_functions():
 def test_header_declares_the_entry_points():
     names = header_functions()
     for n in ("attn_fwd", "attn_bwd", "attn_paged_decode", "attn_paged_gather", "attn_paged_append",
-              "attn_ring_fwd", "attn_comm_init", "attn_comm_destroy"):
+              "attn_lse_merge"):
         assert n in names
 
 
@@ -49,8 +49,7 @@ def test_ctypes_layout_matches_c_compiler(tmp_path):
     if shutil.which("gcc") is None:
         pytest.skip("gcc not available")
     structs = {"attn_mask_t": _lib.AttnMask, "attn_fwd_params_t": _lib.FwdParams,
-               "attn_bwd_params_t": _lib.BwdParams, "attn_paged_params_t": _lib.PagedParams,
-               "attn_ring_params_t": _lib.RingParams}
+               "attn_bwd_params_t": _lib.BwdParams, "attn_paged_params_t": _lib.PagedParams}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{ROOT}/include/attnb200.h"',
              "int main(void) {"]
     for cname, py in structs.items():
