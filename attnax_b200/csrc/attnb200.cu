@@ -11,6 +11,7 @@
 #include "../../include/attnb200.h"
 #include "attn_common.cuh"
 #include "flash_fwd_sm100.cu"
+#include "flash_fwd2_sm100.cu"
 #include "flash_simt.cu"
 #include "flash_bwd_sm100.cu"
 #include "paged.cu"
@@ -193,8 +194,50 @@ static int launch_simt_fwd(const attn_fwd_params_t* p, float* lse, cudaStream_t 
 }
 
 template <int D, bool BF16>
+static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2* dq_t, const int2* dkv_t,
+                             cudaStream_t st) {
+  CUtensorMap tq, tk, tv;
+  if (!make_tmap(&tq, p->dtype, p->q, p->batch, p->num_heads_q, p->seq_q, D, p->q_strides, fwd2::BM) ||
+      !make_tmap(&tk, p->dtype, p->k, p->batch, p->num_heads_kv, p->seq_kv, D, p->k_strides, fwd2::BN) ||
+      !make_tmap(&tv, p->dtype, p->v, p->batch, p->num_heads_kv, p->seq_kv, D, p->v_strides, fwd2::BN))
+    return ATTN_ERR_INVALID;
+  fwd2::Args a;
+  a.B = p->batch; a.Hq = p->num_heads_q; a.Hkv = p->num_heads_kv; a.Sq = p->seq_q; a.Skv = p->seq_kv;
+  a.group = p->num_heads_q / p->num_heads_kv;
+  a.n_ctas = (p->seq_q + 2 * fwd2::BM - 1) / (2 * fwd2::BM);
+  a.sl2 = p->softmax_scale * kLog2e;
+  a.out = p->out;
+  a.o_s0 = p->o_strides[0]; a.o_s1 = p->o_strides[1]; a.o_s2 = p->o_strides[2];
+  a.lse = lse; a.mask = p->mask;
+  a.doc_q_tiles = dq_t; a.doc_kv_tiles = dkv_t;
+  a.nq_doc = (p->seq_q + kDocTile - 1) / kDocTile;
+  a.nk_doc = (p->seq_kv + kDocTile - 1) / kDocTile;
+  constexpr int smem = fwd2::Cfg<D>::SMEM;
+  auto kern = fwd2::flash_fwd2_kernel<D, BF16>;
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    // The in-kernel register split assumes this exact launch register count.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != fwd2::kLaunchRegs)
+      return ATTN_ERR_UNSUPPORTED;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return ATTN_ERR_CUDA;
+    attr_dev = dev;
+  }
+  dim3 grid(a.n_ctas, p->num_heads_q, p->batch);
+  kern<<<grid, fwd2::kThreads, smem, st>>>(tq, tk, tv, a);
+  return launch_status();
+}
+
+template <int D, bool BF16>
 static int launch_sm100_fwd(const attn_fwd_params_t* p, float* lse, const int2* dq_t, const int2* dkv_t,
                             cudaStream_t st) {
+  if (p->seq_q > fwd::BM) {
+    const int rc = launch_sm100_fwd2<D, BF16>(p, lse, dq_t, dkv_t, st);
+    if (rc != ATTN_ERR_UNSUPPORTED) return rc;
+  }
   CUtensorMap tq, tk, tv;
   if (!make_tmap(&tq, p->dtype, p->q, p->batch, p->num_heads_q, p->seq_q, D, p->q_strides, fwd::BM) ||
       !make_tmap(&tk, p->dtype, p->k, p->batch, p->num_heads_kv, p->seq_kv, D, p->k_strides, fwd::BN) ||
@@ -213,11 +256,13 @@ static int launch_sm100_fwd(const attn_fwd_params_t* p, float* lse, const int2* 
   a.nk_doc = (p->seq_kv + kDocTile - 1) / kDocTile;
   constexpr int smem = fwd::Cfg<D>::SMEM;
   auto kern = fwd::flash_fwd_kernel<D, BF16>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return ATTN_ERR_CUDA;
-    attr_set = true;
+    attr_dev = dev;
   }
   dim3 grid(a.nq_tiles, p->num_heads_q, p->batch);
   kern<<<grid, fwd::kThreads, smem, st>>>(tq, tk, tv, a);

@@ -1,0 +1,387 @@
+// Flash-attention forward, two query tiles per CTA (sm_100a).
+//
+// Same function as fwd::flash_fwd_kernel (the forward of flash_attention /
+// pallas_flash_attention, attnax/kernels/attention.py:209-283 and
+// attnax/kernels/pallas.py:118-244), organised so the tensor core never
+// waits on one softmax:
+//   * CTA = two 128-row query tiles (A, B) of one (batch, query head) that
+//     share every K/V tile the TMA warp loads;
+//   * warps 0-3 run the softmax of tile A, warps 4-7 of tile B, warp 8 issues
+//     TMA, warp 9 issues tcgen05.mma (warps 10-11 complete the warpgroup that
+//     hands its registers to the softmax warpgroups);
+//   * TMEM: S_A [0,128), S_B [128,256), O_A [256, 256+D), O_B after it.  P
+//     (bf16/f16) is written back over the first 64 columns of its S and the
+//     PV product reads it straight from TMEM (tcgen05.mma with A in TMEM);
+//   * tensor-core order S_A(j), S_B(j), PV_A(j), S_A(j+1), PV_B(j), S_B(j+1),
+//     so each softmax overlaps two GEMMs of the other tile;
+//   * O is rescaled only when a row maximum grows by more than 2^8 (the
+//     stale maximum keeps P <= 256, exact after the final 1/l);
+//   * a quarter of the exponentials use a cubic polynomial on the FMA pipe
+//     (2^x = 2^n * p(f), n = round(x), |f| <= 1/2, coefficients fitted for
+//     this kernel) so the MUFU pipe is not the bound.
+#include <cfloat>
+
+#include "attn_common.cuh"
+#include "sm100.cuh"
+
+namespace attnb200 {
+namespace fwd2 {
+
+constexpr int BM = 128, BN = 128;
+constexpr int kThreads = 384;      // 3 warpgroups: softmax A, softmax B, TMA + MMA (+2 idle warps)
+// Register split (setmaxnreg): launched at kLaunchRegs per thread; the TMA/MMA
+// warpgroup gives registers up, the softmax warpgroups take them:
+// 128 * kProducerRegs + 256 * kSoftmaxRegs == 384 * kLaunchRegs.
+constexpr int kLaunchRegs = 168, kProducerRegs = 88, kSoftmaxRegs = 208;
+static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs == kThreads * kLaunchRegs, "register split");
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+template <int D>
+struct Cfg {
+  static constexpr int KCH = D / 64;
+  static constexpr int STAGES = (D == 64) ? 4 : 2;
+  static constexpr int Q_BYTES = KCH * BM * 128;  // one query tile
+  static constexpr int KV_BYTES = KCH * BN * 128;
+  static constexpr int OFF_Q = 0;                  // Q_A, Q_B
+  static constexpr int OFF_K = 2 * Q_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
+  static constexpr int NBAR = 1 + 3 * STAGES + 6;
+  static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  __host__ __device__ static constexpr uint32_t s_col(int x) { return x ? 128u : 0u; }
+  __host__ __device__ static constexpr uint32_t o_col(int x) { return x ? 256u + D : 256u; }
+};
+
+struct Args {
+  int B, Hq, Hkv, Sq, Skv, group, n_ctas;
+  float sl2;
+  void* out;
+  long long o_s0, o_s1, o_s2;
+  float* lse;
+  attn_mask_t mask;
+  const int2* doc_q_tiles;
+  const int2* doc_kv_tiles;
+  int nq_doc, nk_doc;
+};
+
+// Cubic fit of 2^f on [-1/2, 1/2] (max relative error 7.6e-5), our own fit.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float y = x + 12582912.f;  // 1.5 * 2^23: the rounded integer lands in the low mantissa bits
+  const float f = x - (y - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05517084f, f, 0.24260935f), f, 0.69326097f), f, 0.99992818f);
+  return __int_as_float(__float_as_int(p) + ((__float_as_int(y) - 0x4B400000) << 23));
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Args a) {
+  using C = Cfg<D>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t sb = (raw_base + 1023u) & ~1023u;
+  uint8_t* sp = smem_raw + (sb - raw_base);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ct = a.n_ctas - 1 - (int)blockIdx.x;  // heavy (late) tiles first
+  const int hq = blockIdx.y, b = blockIdx.z;
+  const int hkv = hq / a.group;
+  int q0[2], q1[2];
+  bool act[2];
+  for (int x = 0; x < 2; ++x) {
+    q0[x] = ct * 2 * BM + x * BM;
+    q1[x] = min(q0[x] + BM, a.Sq);
+    act[x] = q0[x] < a.Sq;
+  }
+
+  const uint32_t bar0 = sb + C::OFF_BAR;
+  const uint32_t q_full = bar0;
+  auto k_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto v_full = [&](int s) { return bar0 + 8u * (1 + S + s); };
+  auto kv_empty = [&](int s) { return bar0 + 8u * (1 + 2 * S + s); };
+  auto s_full = [&](int x) { return bar0 + 8u * (1 + 3 * S + x); };
+  auto p_full = [&](int x) { return bar0 + 8u * (3 + 3 * S + x); };
+  auto o_done = [&](int x) { return bar0 + 8u * (5 + 3 * S + x); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sp + C::OFF_TMEMPTR);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(s_full(x), 1);
+      mbar_init(p_full(x), 128);
+      mbar_init(o_done(x), 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Union of the two tiles' kv ranges; per-tile state of each kv tile.
+  int jl[2], jh[2];
+  for (int x = 0; x < 2; ++x) {
+    if (act[x]) band_tile_range(a.mask, q0[x], q1[x], a.Skv, BN, &jl[x], &jh[x]);
+    else jl[x] = jh[x] = 0;
+  }
+  const int j_lo = act[1] ? min(jl[0], jl[1]) : jl[0];
+  const int j_hi = act[1] ? max(jh[0], jh[1]) : jh[0];
+  auto state_of = [&](int x, int j) {
+    if (!act[x] || j < jl[x] || j >= jh[x]) return (int)kSkip;
+    return tile_state(a.mask, a.doc_q_tiles, a.doc_kv_tiles, a.nq_doc, a.nk_doc, b, q0[x], q1[x], j * BN,
+                      min((j + 1) * BN, a.Skv), BN);
+  };
+
+  if (warp >= 8) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+   if (warp == 8) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_expect_tx(q_full, 2 * C::Q_BYTES);
+      for (int x = 0; x < 2; ++x)
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sb + C::OFF_Q + x * C::Q_BYTES + c * BM * 128, &tm_q, q_full, c * 64, q0[x], hq, b);
+      int n = 0;
+      for (int j = j_lo; j < j_hi; ++j) {
+        if (state_of(0, j) == kSkip && state_of(1, j) == kSkip) continue;
+        const int s = n % S;
+        if (!mbar_wait(kv_empty(s), ((n / S) & 1) ^ 1, kStatusTimeoutLoad)) break;
+        mbar_expect_tx(k_full(s), C::KV_BYTES);
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sb + C::OFF_K + s * C::KV_BYTES + c * BN * 128, &tm_k, k_full(s), c * 64, j * BN, hkv, b);
+        mbar_expect_tx(v_full(s), C::KV_BYTES);
+        for (int c = 0; c < C::KCH; ++c)
+          tma_load_4d(sb + C::OFF_V + s * C::KV_BYTES + c * BN * 128, &tm_v, v_full(s), c * 64, j * BN, hkv, b);
+        ++n;
+      }
+    }
+   } else if (warp == 9) {
+    // ----------------------------------------------------------------- MMA --
+    if (lane == 0) {
+      constexpr int FMT = BF16 ? 1 : 0;
+      constexpr uint32_t IDESC_QK = idesc_f16(128, BN, FMT, 0, 0);
+      constexpr uint32_t IDESC_PV = idesc_f16(128, D, FMT, 0, 1);
+      bool ok = mbar_wait(q_full, 0, kStatusTimeoutMma);
+      int it[2] = {0, 0};      // S products issued per tile
+      int pv[2] = {0, 0};      // PV products issued per tile
+      int prev_s = -1, n = 0;  // stage of the previous kv tile, kv tiles consumed
+      bool prev_act[2] = {false, false};
+      auto issue_s = [&](int x, int s) {
+        const uint32_t d = tmem + C::s_col(x);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint64_t ad =
+              sdesc_sw128(sb + C::OFF_Q + x * C::Q_BYTES + (k >> 2) * BM * 128 + (k & 3) * 32, 16, 1024);
+          const uint64_t bd =
+              sdesc_sw128(sb + C::OFF_K + s * C::KV_BYTES + (k >> 2) * BN * 128 + (k & 3) * 32, 16, 1024);
+          umma_f16(d, ad, bd, IDESC_QK, k > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full(x));
+        ++it[x];
+      };
+      auto issue_pv = [&](int x, int s) -> bool {
+        if (!mbar_wait(p_full(x), pv[x] & 1, kStatusTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t pa = tmem + C::s_col(x);  // P: bf16 pairs in the first 64 columns of S
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k) {
+          const uint64_t bd = sdesc_sw128(sb + C::OFF_V + s * C::KV_BYTES + k * 16 * 128, BN * 128, 1024);
+          asm volatile(
+              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+              " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem + C::o_col(x)),
+              "r"(pa + (uint32_t)(k * 8)), "l"(bd), "r"(IDESC_PV), "r"((pv[x] > 0 || k > 0) ? 1u : 0u)
+              : "memory");
+        }
+        umma_commit(o_done(x));
+        ++pv[x];
+        return true;
+      };
+      for (int j = j_lo; ok && j < j_hi; ++j) {
+        const bool ax = state_of(0, j) != kSkip, bx = state_of(1, j) != kSkip;
+        if (!ax && !bx) continue;
+        const int s = n % S;
+        ok = mbar_wait(k_full(s), (n / S) & 1, kStatusTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        if (prev_s >= 0) ok = mbar_wait(v_full(prev_s), ((n - 1) / S) & 1, kStatusTimeoutMma);
+        if (!ok) break;
+        if (prev_act[0]) ok = issue_pv(0, prev_s);
+        if (ok && ax) issue_s(0, s);
+        if (ok && prev_act[1]) ok = issue_pv(1, prev_s);
+        if (ok && bx) issue_s(1, s);
+        if (!ok) break;
+        if (prev_s >= 0) umma_commit(kv_empty(prev_s));
+        prev_s = s;
+        prev_act[0] = ax;
+        prev_act[1] = bx;
+        ++n;
+      }
+      if (ok && prev_s >= 0) {
+        ok = mbar_wait(v_full(prev_s), ((n - 1) / S) & 1, kStatusTimeoutMma);
+        if (ok && prev_act[0]) ok = issue_pv(0, prev_s);
+        if (ok && prev_act[1]) ok = issue_pv(1, prev_s);
+        if (ok) umma_commit(kv_empty(prev_s));
+      }
+    }
+   }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    // ------------------------------------------------------------- softmax --
+    const int x = warp >> 2;         // query tile of this warpgroup
+    const int r = threadIdx.x & 127; // row within the tile == TMEM lane
+    const int my_q0 = x ? q0[1] : q0[0];
+    const bool my_act = x ? act[1] : act[0];
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    float m_run = -FLT_MAX, l_run = 0.f;
+    int i = 0;
+    bool ok = true;
+    for (int j = j_lo; j < j_hi; ++j) {
+      const int st = state_of(x, j);
+      if (st == kSkip) continue;
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), i & 1, kStatusTimeoutSoftmax));
+      if (!ok) break;
+      tc_fence_after();
+      const int k0 = j * BN;
+      const uint32_t s_addr = tmem + lane_base + C::s_col(x);
+      if (st == kPartial) {
+        // Boundary tile: mask/transform 32 columns at a time in TMEM so the
+        // per-column mask state never competes with the 128 scores.
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t raw[32];
+          float t[32];
+          tmem_ld32(s_addr + c * 32, raw);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) t[e] = __uint_as_float(raw[e]);
+          const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, my_q0 + r, k0 + c * 32,
+                                         max(0, min(32, a.Skv - (k0 + c * 32))), false);
+          transform_row<32>(t, rc, true);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(t[e]);
+          tmem_st32(s_addr + c * 32, raw);
+        }
+        tmem_wait_st();
+      }
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(s_addr + c * 32, raw);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(raw[e]);
+      }
+      tmem_wait_ld();
+      if (st != kPartial) {
+        const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, my_q0 + r, k0, BN, false);
+        transform_row<BN>(s, rc, false);
+      }
+      float mx = -FLT_MAX;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      float alpha = 1.f;
+      if (mx > m_run + kRescaleThreshold) {
+        alpha = ex2(m_run - mx);
+        m_run = mx;
+      }
+      const float neg_m = -m_run;
+      float sum = 0.f;
+      // P in two 64-column halves so the S registers die as P is stored.
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const int cc = h * 64 + c;
+          const float p0 = ex2(s[cc] + neg_m);
+          const float p1 = (c & 2) ? exp2_poly(s[cc + 1] + neg_m) : ex2(s[cc + 1] + neg_m);
+          sum += p0 + p1;
+          pk[c >> 1] = pack2(p0, p1, BF16);
+        }
+        tmem_st32(tmem + lane_base + C::s_col(x) + h * 32, pk);
+      }
+      l_run = l_run * alpha + sum;
+      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // PV of the previous tile must be complete before O is rescaled.
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done(x), (i - 1) & 1, kStatusTimeoutSoftmax));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          const uint32_t ta = tmem + lane_base + C::o_col(x) + c * 32;
+          tmem_ld32(ta, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(ta, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full(x));
+      ++i;
+    }
+    // ------------------------------------------------------------ epilogue --
+    if (ok && i > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done(x), (i - 1) & 1, kStatusTimeoutSoftmax));
+    if (ok && my_act) {
+      tc_fence_after();
+      const bool row_ok = (my_q0 + r) < a.Sq;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* orow = reinterpret_cast<T*>(a.out) + (long long)b * a.o_s0 + (long long)hq * a.o_s1 +
+                (long long)(my_q0 + r) * a.o_s2;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (i > 0) {
+          tmem_ld32(tmem + lane_base + C::o_col(x) + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv, BF16);
+            w.y = pack2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv, BF16);
+            w.z = pack2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv, BF16);
+            w.w = pack2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv, BF16);
+            *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = w;
+          }
+        }
+      }
+      if (row_ok && a.lse)
+        a.lse[((long long)b * a.Hq + hq) * a.Sq + my_q0 + r] =
+            (m_run == -FLT_MAX || l_run <= 0.f) ? -INFINITY : (m_run + lg2(l_run)) * kLn2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace fwd2
+}  // namespace attnb200
