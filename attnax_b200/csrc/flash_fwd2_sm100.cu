@@ -16,9 +16,10 @@
 //     so each softmax overlaps two GEMMs of the other tile;
 //   * O is rescaled only when a row maximum grows by more than 2^8 (the
 //     stale maximum keeps P <= 256, exact after the final 1/l);
-//   * a quarter of the exponentials use a cubic polynomial on the FMA pipe
-//     (2^x = 2^n * p(f), n = round(x), |f| <= 1/2, coefficients fitted for
-//     this kernel) so the MUFU pipe is not the bound.
+//   * one exponential in ATTN_FWD2_POLY_EVERY uses a cubic polynomial on the
+//     FMA pipe (2^x = 2^n * p(f), n = round(x), |f| <= 1/2, coefficients
+//     fitted for this kernel) to take load off the MUFU pipe;
+//   * scale/ALiBi/exp-argument/row-sum arithmetic runs as packed f32x2 ops.
 #include <cfloat>
 
 #include "attn_common.cuh"
@@ -35,6 +36,15 @@ constexpr int kThreads = 384;      // 3 warpgroups: softmax A, softmax B, TMA + 
 constexpr int kLaunchRegs = 168, kProducerRegs = 88, kSoftmaxRegs = 208;
 static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs == kThreads * kLaunchRegs, "register split");
 constexpr float kRescaleThreshold = 8.f;  // log2 units
+#ifndef ATTN_FWD2_REG_PARTIAL
+#define ATTN_FWD2_REG_PARTIAL 0  // band/prefix boundary tiles masked in registers (else via TMEM chunks)
+#endif
+#ifndef ATTN_FWD2_MAX3
+#define ATTN_FWD2_MAX3 0  // three-input max in the row-max tree
+#endif
+#ifndef ATTN_FWD2_POLY_EVERY
+#define ATTN_FWD2_POLY_EVERY 0  // one exponential in this many uses the FMA-pipe polynomial (0: none)
+#endif
 
 template <int D>
 struct Cfg {
@@ -251,6 +261,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_run = -FLT_MAX, l_run = 0.f;
     int i = 0;
     bool ok = true;
+    // Per-CTA constants of the full-tile path (no per-tile global loads).
+    const bool has_alibi = a.mask.alibi_slopes != nullptr;
+    const float slope_l2 = has_alibi ? a.mask.alibi_slopes[hq] * kLog2e : 0.f;
+    // With a causal band every kept score has q >= kv, so |q - kv| = q - kv
+    // and ALiBi is linear in the column: t = s*sl2 + slope*(c - d0).
+    const bool linear_alibi = has_alibi && a.mask.has_band && a.mask.band_lo >= 0;
+    const long long qg_row = a.mask.q_offset + my_q0 + r;
+    // Bias, boolean and document masks need per-column loads: their boundary
+    // tiles go through TMEM in 32-column chunks.  Band/prefix boundaries are
+    // masked in registers.
+    const bool complex_mask = !ATTN_FWD2_REG_PARTIAL || a.mask.bias || a.mask.bool_mask || a.mask.doc_q;
+    const int band_lo = a.mask.has_band ? clamp_i32(a.mask.band_lo) : -(1 << 30);
+    const int band_hi = a.mask.has_band ? clamp_i32(a.mask.band_hi) : (1 << 30);
+    const long long pref = a.mask.prefix_len ? (long long)a.mask.prefix_len[b] : -1;
     for (int j = j_lo; j < j_hi; ++j) {
       const int st = state_of(x, j);
       if (st == kSkip) continue;
@@ -259,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int k0 = j * BN;
       const uint32_t s_addr = tmem + lane_base + C::s_col(x);
-      if (st == kPartial) {
+      if (st == kPartial && complex_mask) {
         // Boundary tile: mask/transform 32 columns at a time in TMEM so the
         // per-column mask state never competes with the 128 scores.
 #pragma unroll 1
@@ -279,29 +303,101 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
       }
+      // Scores into registers: the second half loads while the first is processed.
       float s[BN];
+      float mxp[8];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(s_addr + c * 32, raw);
+      for (int e = 0; e < 8; ++e) mxp[e] = -FLT_MAX;
+      // Mode: 0 = already transformed (complex boundary), 1 = plain scale (full
+      // tile, scale folded into exp2), 2 = linear ALiBi, 3 = general ALiBi,
+      // 4 = plain scale applied before masking (band/prefix boundary).
+      const bool part = st == kPartial;
+      const int mode = (part && complex_mask) ? 0
+                       : (!has_alibi ? (part ? 4 : 1) : (linear_alibi ? 2 : 3));
+      const int d0 = clamp_i32(qg_row - (a.mask.kv_offset + k0));
+      const float fd0 = (float)d0;
+      const float base = -slope_l2 * fd0;
+      const int ncols = min(BN, a.Skv - k0);
+      const int pref_cols = (int)ll_max(-1, ll_min((long long)BN, pref - (a.mask.kv_offset + k0)));
 #pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(raw[e]);
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(s_addr + (h * 2 + c) * 32, raw);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[(h * 2 + c) * 32 + e] = __uint_as_float(raw[e]);
+        }
+        tmem_wait_ld();
+        if (mode == 2) {
+          // t = s*sl2 + (base + slope*c), pairs of columns per f32x2 op; the
+          // additive term advances by 8*slope along 4 independent chains.
+          const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2);
+          const unsigned long long step = f2_pack(8.f * slope_l2, 8.f * slope_l2);
+          unsigned long long addv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int c = h * 64 + 2 * q;
+            addv[q] = f2_pack(fmaf(slope_l2, (float)c, base), fmaf(slope_l2, (float)(c + 1), base));
+          }
+#pragma unroll
+          for (int c = h * 64; c < h * 64 + 64; c += 2) {
+            const int q = (c >> 1) & 3;
+            float lo, hi;
+            f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, addv[q]), lo, hi);
+            s[c] = lo;
+            s[c + 1] = hi;
+            addv[q] = f2_add(addv[q], step);
+          }
+        } else if (mode == 3) {
+#pragma unroll
+          for (int c = h * 64; c < h * 64 + 64; ++c) s[c] = fmaf(-slope_l2, fabsf(fd0 - (float)c), s[c] * a.sl2);
+        } else if (mode == 4) {
+          const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2), z = f2_pack(0.f, 0.f);
+#pragma unroll
+          for (int c = h * 64; c < h * 64 + 64; c += 2) {
+            float lo, hi;
+            f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, z), lo, hi);
+            s[c] = lo;
+            s[c + 1] = hi;
+          }
+        }
+        if (part && !complex_mask) {
+          // keep iff band_lo <= q - kv <= band_hi and (kv < prefix or kv <= q); pad columns are -inf
+#pragma unroll
+          for (int c = h * 64; c < h * 64 + 64; ++c) {
+            const int d = d0 - c;
+            const bool keep = d >= band_lo && d <= band_hi && (c < pref_cols || d >= 0 || pref < 0);
+            s[c] = c < ncols ? (keep ? s[c] : -FLT_MAX) : -INFINITY;
+          }
+        }
+#if ATTN_FWD2_MAX3
+#pragma unroll
+        for (int c = h * 64; c < h * 64 + 64; c += 2) {
+          float m3;
+          asm("max.f32 %0, %1, %2, %3;" : "=f"(m3) : "f"(mxp[(c >> 1) & 7]), "f"(s[c]), "f"(s[c + 1]));
+          mxp[(c >> 1) & 7] = m3;
+        }
+#else
+#pragma unroll
+        for (int c = h * 64; c < h * 64 + 64; ++c) mxp[c & 7] = fmaxf(mxp[c & 7], s[c]);
+#endif
       }
-      tmem_wait_ld();
-      if (st != kPartial) {
-        const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, my_q0 + r, k0, BN, false);
-        transform_row<BN>(s, rc, false);
-      }
-      float mx = -FLT_MAX;
-#pragma unroll
-      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      // Plain tiles were maxed on raw scores; the scale is applied inside exp2 below.
+      const float sc = (mode == 1) ? a.sl2 : 1.f;
+      if (mode == 1) mx *= a.sl2;
       float alpha = 1.f;
       if (mx > m_run + kRescaleThreshold) {
         alpha = ex2(m_run - mx);
         m_run = mx;
       }
       const float neg_m = -m_run;
-      float sum = 0.f;
+      unsigned long long sp[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sp[e] = f2_pack(0.f, 0.f);
+      const unsigned long long sc2 = f2_pack(sc, sc), negm2 = f2_pack(neg_m, neg_m);
       // P in two 64-column halves so the S registers die as P is stored.
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -309,12 +405,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 64; c += 2) {
           const int cc = h * 64 + c;
-          const float p0 = ex2(s[cc] + neg_m);
-          const float p1 = (c & 2) ? exp2_poly(s[cc + 1] + neg_m) : ex2(s[cc + 1] + neg_m);
-          sum += p0 + p1;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(s[cc], s[cc + 1]), sc2, negm2), x0, x1);
+          const float p0 = ex2(x0);
+          const float p1 = (ATTN_FWD2_POLY_EVERY > 0 && ((c >> 1) % (ATTN_FWD2_POLY_EVERY > 0 ? ATTN_FWD2_POLY_EVERY / 2 : 1)) ==
+                            (ATTN_FWD2_POLY_EVERY > 0 ? ATTN_FWD2_POLY_EVERY / 2 - 1 : 0))
+                               ? exp2_poly(x1)
+                               : ex2(x1);
+          sp[(c >> 1) & 3] = f2_add(sp[(c >> 1) & 3], f2_pack(p0, p1));
           pk[c >> 1] = pack2(p0, p1, BF16);
         }
         tmem_st32(tmem + lane_base + C::s_col(x) + h * 32, pk);
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float lo, hi;
+        f2_unpack(sp[e], lo, hi);
+        sum += lo + hi;
       }
       l_run = l_run * alpha + sum;
       if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
