@@ -14,8 +14,11 @@
 //   dq:   CTA = 128 q rows of one (batch, query head).  Loops over 64-row kv
 //         tiles:  S = Q K^T, dP = dO V^T, dQ += dS K.
 //
-// Warp roles in both: warps 0-3 own one TMEM lane/row each (elementwise math
-// and epilogue), warp 4 issues TMA, warp 5 allocates TMEM and issues MMAs.
+// Warp roles in both: warps 0-7 do the elementwise math and the epilogue --
+// warps w and w+4 share TMEM lanes 32*(w%4).. (one row per thread) and split
+// the tile's columns in halves, so two warps per sub-partition hide each
+// other's latency (no row reductions are needed: P uses the forward LSE);
+// warp 8 issues TMA, warp 9 allocates TMEM and issues MMAs.
 #include <cfloat>
 
 #include "attn_common.cuh"
@@ -24,7 +27,7 @@
 namespace attnb200 {
 namespace bwd {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warps 0-7 elementwise (two per TMEM lane group), 8 TMA, 9 MMA
 constexpr int KROWS = 128;  // kv rows per dkdv CTA (MMA M)
 constexpr int QT = 64;      // q rows per dkdv iteration (MMA N)
 constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
@@ -122,14 +125,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 128);
+      mbar_init(s_free(i), 256);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(p_free, 1);
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     return tile_state(a.mask, nullptr, nullptr, 0, 0, b, q0, min(q0 + QT, a.Sq), k0, k1, KROWS);
   };
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -178,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++i;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       constexpr int FMT = BF16 ? 1 : 0;
       constexpr uint32_t ID_S = idesc_f16(128, QT, FMT, 0, 0);
@@ -228,9 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && i > 0) ok = issue_grads(i - 1);
       umma_commit(acc_done);
     }
-  } else {
-    const int r = threadIdx.x;  // kv row within the tile == TMEM lane
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  } else if (warp < 8) {
+    const int r = threadIdx.x & 127;  // kv row within the tile == TMEM lane
+    const int half = warp >> 2;       // columns [32*half, 32*half + 32) of each q tile
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     uint8_t* PT = sp + C::OFF_P;
     uint8_t* DST = sp + C::OFF_DS;
     int i = 0;
@@ -244,24 +248,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, kStatusTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-      float sc[QT], dp[QT];
-#pragma unroll
-      for (int c = 0; c < QT / 32; ++c) {
-        tmem_ld32(tmem + lane_base + C::COL_S + (i & 1) * QT + c * 32,
-                  *reinterpret_cast<uint32_t(*)[32]>(&sc[c * 32]));
-        tmem_ld32(tmem + lane_base + C::COL_DP + (i & 1) * QT + c * 32,
-                  *reinterpret_cast<uint32_t(*)[32]>(&dp[c * 32]));
-      }
+      constexpr int HC = QT / 2;  // columns per thread
+      float sc[HC], dp[HC];
+      tmem_ld32(tmem + lane_base + C::COL_S + (i & 1) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(sc));
+      tmem_ld32(tmem + lane_base + C::COL_DP + (i & 1) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(dp));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(s_free(i & 1));
-      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, k0 + r, q0, min(QT, a.Sq - q0), true);
-      transform_row<QT>(sc, rc, st == kPartial || k0 + r >= a.Skv);
-      const float* sl = reinterpret_cast<const float*>(sp + C::OFF_ST + s * C::STAGE + 2 * C::QD_BYTES);
+      const int c0 = q0 + half * HC;
+      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, k0 + r, c0, max(0, min(HC, a.Sq - c0)), true);
+      transform_row<HC>(sc, rc, st == kPartial || k0 + r >= a.Skv);
+      const float* sl = reinterpret_cast<const float*>(sp + C::OFF_ST + s * C::STAGE + 2 * C::QD_BYTES) + half * HC;
       const float* sd = sl + QT;
       const bool row_ok = k0 + r < a.Skv;
 #pragma unroll
-      for (int c = 0; c < QT; ++c) {
+      for (int c = 0; c < HC; ++c) {
         const float p = row_ok ? ex2(sc[c] - sl[c]) : 0.f;
         sc[c] = p;
         dp[c] = p * (dp[c] - sd[c]);
@@ -271,14 +272,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
       }
 #pragma unroll
-      for (int u = 0; u < QT / 8; ++u) {
+      for (int u = 0; u < HC / 8; ++u) {
         const int c = u * 8;
         uint4 pv, dv;
         pv.x = pack2(sc[c], sc[c + 1], BF16); pv.y = pack2(sc[c + 2], sc[c + 3], BF16);
         pv.z = pack2(sc[c + 4], sc[c + 5], BF16); pv.w = pack2(sc[c + 6], sc[c + 7], BF16);
         dv.x = pack2(dp[c], dp[c + 1], BF16); dv.y = pack2(dp[c + 2], dp[c + 3], BF16);
         dv.z = pack2(dp[c + 4], dp[c + 5], BF16); dv.w = pack2(dp[c + 6], dp[c + 7], BF16);
-        const int off = r * 128 + ((u ^ (r & 7)) << 4);
+        const int off = r * 128 + (((half * (HC / 8) + u) ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(PT + off) = pv;
         *reinterpret_cast<uint4*>(DST + off) = dv;
       }
@@ -295,12 +296,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       T* dvr = reinterpret_cast<T*>(a.dv) + b * a.dv_s[0] + hkv * a.dv_s[1] + (long long)(k0 + r) * a.dv_s[2];
       T* dkr = reinterpret_cast<T*>(a.dk) + b * a.dk_s[0] + hkv * a.dk_s[1] + (long long)(k0 + r) * a.dk_s[2];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        T* dst = half ? dkr : dvr;
-        const uint32_t col = half ? C::COL_DK : C::COL_DV;
-        const float mul = half ? a.scale : 1.f;
+      for (int which = 0; which < 2; ++which) {
+        T* dst = which ? dkr : dvr;
+        const uint32_t col = which ? C::COL_DK : C::COL_DV;
+        const float mul = which ? a.scale : 1.f;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
           uint32_t o[32];
           if (i > 0) {
             tmem_ld32(tmem + lane_base + col + c * 32, o);
@@ -326,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
@@ -389,14 +390,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 128);
+      mbar_init(s_free(i), 256);
     }
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, 256);
     mbar_init(ds_free, 1);
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -411,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     return tile_state(a.mask, nullptr, nullptr, 0, 0, b, q0, q1, j * KT, min((j + 1) * KT, a.Skv), KT);
   };
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -436,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++i;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       constexpr int FMT = BF16 ? 1 : 0;
       constexpr uint32_t ID_S = idesc_f16(128, KT, FMT, 0, 0);
@@ -483,9 +484,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && i > 0) ok = issue_dq(i - 1);
       umma_commit(acc_done);
     }
-  } else {
-    const int r = threadIdx.x;  // q row within the tile == TMEM lane
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  } else if (warp < 8) {
+    const int r = threadIdx.x & 127;  // q row within the tile == TMEM lane
+    const int half = warp >> 2;       // columns [32*half, 32*half + 32) of each kv tile
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const bool row_ok = q0 + r < a.Sq;
     const long long ridx = ((long long)b * a.Hq + hq) * a.Sq_pad + q0 + r;
     const float lse2 = a.lse2[ridx], delta = a.delta[ridx];
@@ -498,22 +500,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, kStatusTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-      float sc[KT], dp[KT];
-#pragma unroll
-      for (int c = 0; c < KT / 32; ++c) {
-        tmem_ld32(tmem + lane_base + C::COL_S + (i & 1) * KT + c * 32,
-                  *reinterpret_cast<uint32_t(*)[32]>(&sc[c * 32]));
-        tmem_ld32(tmem + lane_base + C::COL_DP + (i & 1) * KT + c * 32,
-                  *reinterpret_cast<uint32_t(*)[32]>(&dp[c * 32]));
-      }
+      constexpr int HC = KT / 2;  // columns per thread
+      float sc[HC], dp[HC];
+      tmem_ld32(tmem + lane_base + C::COL_S + (i & 1) * KT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(sc));
+      tmem_ld32(tmem + lane_base + C::COL_DP + (i & 1) * KT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(dp));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(s_free(i & 1));
-      const int k0 = j * KT;
-      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, k0, min(KT, a.Skv - k0), false);
-      transform_row<KT>(sc, rc, st == kPartial);
+      const int c0 = j * KT + half * HC;
+      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, c0, max(0, min(HC, a.Skv - c0)), false);
+      transform_row<HC>(sc, rc, st == kPartial);
 #pragma unroll
-      for (int c = 0; c < KT; ++c) {
+      for (int c = 0; c < HC; ++c) {
         const float p = ex2(sc[c] - lse2);
         dp[c] = p * (dp[c] - delta);
       }
@@ -522,12 +520,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
       }
 #pragma unroll
-      for (int u = 0; u < KT / 8; ++u) {
+      for (int u = 0; u < HC / 8; ++u) {
         const int c = u * 8;
         uint4 w;
         w.x = pack2(dp[c], dp[c + 1], BF16); w.y = pack2(dp[c + 2], dp[c + 3], BF16);
         w.z = pack2(dp[c + 4], dp[c + 5], BF16); w.w = pack2(dp[c + 6], dp[c + 7], BF16);
-        *reinterpret_cast<uint4*>(DS + r * 128 + ((u ^ (r & 7)) << 4)) = w;
+        *reinterpret_cast<uint4*>(DS + r * 128 + (((half * (HC / 8) + u) ^ (r & 7)) << 4)) = w;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -540,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       T* dqr = reinterpret_cast<T*>(a.dq) + b * a.dq_s[0] + hq * a.dq_s[1] + (long long)(q0 + r) * a.dq_s[2];
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
         uint32_t o[32];
         if (i > 0) {
           tmem_ld32(tmem + lane_base + C::COL_DQ + c * 32, o);
@@ -565,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
