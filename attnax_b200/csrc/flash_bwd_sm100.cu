@@ -27,6 +27,18 @@
 namespace attnb200 {
 namespace bwd {
 
+#ifndef ATTN_BWD_KV_STAGES
+#define ATTN_BWD_KV_STAGES 3  // dK/dV kernel: Q/dO/lse/delta tiles in flight
+#endif
+#ifndef ATTN_BWD_P_BUFS
+#define ATTN_BWD_P_BUFS 1     // dK/dV kernel: P^T/dS^T shared-memory buffers
+#endif
+#ifndef ATTN_BWD_Q_STAGES
+#define ATTN_BWD_Q_STAGES 4   // dQ kernel: K/V tiles in flight
+#endif
+#ifndef ATTN_BWD_DS_BUFS
+#define ATTN_BWD_DS_BUFS 1    // dQ kernel: dS shared-memory buffers
+#endif
 constexpr int kThreads = 320;  // warps 0-7 elementwise (two per TMEM lane group), 8 TMA, 9 MMA
 constexpr int KROWS = 128;  // kv rows per dkdv CTA (MMA M)
 constexpr int QT = 64;      // q rows per dkdv iteration (MMA N)
@@ -73,17 +85,18 @@ __device__ __forceinline__ void band_q_range(const attn_mask_t& m, int k0, int k
 template <int D>
 struct CfgKV {
   static constexpr int KCH = D / 64;
-  static constexpr int ST = 2;
+  static constexpr int ST = ATTN_BWD_KV_STAGES;
+  static constexpr int PB = ATTN_BWD_P_BUFS;
   static constexpr int KV_BYTES = KCH * KROWS * 128;  // K or V tile
   static constexpr int QD_BYTES = KCH * QT * 128;     // Q or dO tile
   static constexpr int STAGE = ((2 * QD_BYTES + 2 * QT * 4) + 1023) / 1024 * 1024;  // 1024-aligned
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = KV_BYTES;
   static constexpr int OFF_ST = 2 * KV_BYTES;                 // stages: Q, dO, lse2, delta
-  static constexpr int OFF_P = OFF_ST + ST * STAGE;           // P^T  [128 kv][64 q] bf16
-  static constexpr int OFF_DS = OFF_P + KROWS * 128;          // dS^T [128 kv][64 q] bf16
-  static constexpr int OFF_BAR = OFF_DS + KROWS * 128;
-  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 2 + 1;
+  static constexpr int OFF_P = OFF_ST + ST * STAGE;           // P^T  [PB][128 kv][64 q] bf16
+  static constexpr int OFF_DS = OFF_P + PB * KROWS * 128;     // dS^T [PB][128 kv][64 q] bf16
+  static constexpr int OFF_BAR = OFF_DS + PB * KROWS * 128;
+  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + PB + 1;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
@@ -113,8 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto s_full = [&](int i) { return bar0 + 8u * (1 + 2 * ST + i); };
   auto s_free = [&](int i) { return bar0 + 8u * (3 + 2 * ST + i); };
   const uint32_t p_full = bar0 + 8u * (5 + 2 * ST);
-  const uint32_t p_free = bar0 + 8u * (6 + 2 * ST);
-  const uint32_t acc_done = bar0 + 8u * (7 + 2 * ST);
+  auto p_free = [&](int buf) { return bar0 + 8u * (6 + 2 * ST + buf); };
+  const uint32_t acc_done = bar0 + 8u * (6 + 2 * ST + C::PB);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sp + C::OFF_TMEMPTR);
 
   if (threadIdx.x == 0) {
@@ -128,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(s_free(i), 256);
     }
     mbar_init(p_full, 256);
-    mbar_init(p_free, 1);
+    for (int q = 0; q < C::PB; ++q) mbar_init(p_free(q), 1);
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
@@ -194,15 +207,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < QT / 16; ++k) {
-          const uint64_t pa = sdesc_sw128(sb + C::OFF_P + k * 32, 16, 1024);
-          const uint64_t da = sdesc_sw128(sb + C::OFF_DS + k * 32, 16, 1024);
+          const uint64_t pa = sdesc_sw128(sb + C::OFF_P + (j % C::PB) * KROWS * 128 + k * 32, 16, 1024);
+          const uint64_t da = sdesc_sw128(sb + C::OFF_DS + (j % C::PB) * KROWS * 128 + k * 32, 16, 1024);
           const uint64_t dob = sdesc_sw128(base + C::QD_BYTES + k * 16 * 128, QT * 128, 1024);
           const uint64_t qb = sdesc_sw128(base + k * 16 * 128, QT * 128, 1024);
           umma_f16(tmem + C::COL_DV, pa, dob, ID_G, (j > 0 || k > 0) ? 1u : 0u);
           umma_f16(tmem + C::COL_DK, da, qb, ID_G, (j > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(st_free(s));
-        umma_commit(p_free);
+        umma_commit(p_free(j % C::PB));
         return true;
       };
       int i = 0;
@@ -262,13 +275,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* sd = sl + QT;
       const bool row_ok = k0 + r < a.Skv;
 #pragma unroll
-      for (int c = 0; c < HC; ++c) {
-        const float p = row_ok ? ex2(sc[c] - sl[c]) : 0.f;
-        sc[c] = p;
-        dp[c] = p * (dp[c] - sd[c]);
+      for (int c = 0; c < HC; c += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(sl + c);
+        const float4 d4 = *reinterpret_cast<const float4*>(sd + c);
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p = row_ok ? ex2(sc[c + e] - lv[e]) : 0.f;
+          sc[c + e] = p;
+          dp[c + e] = p * (dp[c + e] - dv4[e]);
+        }
       }
-      if (i > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(p_free, (i - 1) & 1, kStatusTimeoutSoftmax));
+      if (i >= C::PB) {  // this buffer was last read by the gradient GEMMs of iteration i - PB
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(p_free(i % C::PB), ((i / C::PB) - 1) & 1, kStatusTimeoutSoftmax));
         if (!ok) break;
       }
 #pragma unroll
@@ -280,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         dv.x = pack2(dp[c], dp[c + 1], BF16); dv.y = pack2(dp[c + 2], dp[c + 3], BF16);
         dv.z = pack2(dp[c + 4], dp[c + 5], BF16); dv.w = pack2(dp[c + 6], dp[c + 7], BF16);
         const int off = r * 128 + (((half * (HC / 8) + u) ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(PT + off) = pv;
-        *reinterpret_cast<uint4*>(DST + off) = dv;
+        *reinterpret_cast<uint4*>(PT + (i % C::PB) * KROWS * 128 + off) = pv;
+        *reinterpret_cast<uint4*>(DST + (i % C::PB) * KROWS * 128 + off) = dv;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -338,15 +358,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 struct CfgQ {
   static constexpr int KCH = D / 64;
-  static constexpr int ST = 3;
+  static constexpr int ST = ATTN_BWD_Q_STAGES;
+  static constexpr int DB = ATTN_BWD_DS_BUFS;
   static constexpr int Q_BYTES = KCH * QROWS * 128;   // Q or dO
   static constexpr int KV_BYTES = KCH * KT * 128;     // K or V tile
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = Q_BYTES;
   static constexpr int OFF_ST = 2 * Q_BYTES;          // stages: K, V
-  static constexpr int OFF_DS = OFF_ST + ST * 2 * KV_BYTES;  // dS [128 q][64 kv] bf16
-  static constexpr int OFF_BAR = OFF_DS + QROWS * 128;
-  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 2 + 1;
+  static constexpr int OFF_DS = OFF_ST + ST * 2 * KV_BYTES;  // dS [DB][128 q][64 kv] bf16
+  static constexpr int OFF_BAR = OFF_DS + DB * QROWS * 128;
+  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + DB + 1;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
@@ -378,8 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto s_full = [&](int i) { return bar0 + 8u * (1 + 2 * ST + i); };
   auto s_free = [&](int i) { return bar0 + 8u * (3 + 2 * ST + i); };
   const uint32_t ds_full = bar0 + 8u * (5 + 2 * ST);
-  const uint32_t ds_free = bar0 + 8u * (6 + 2 * ST);
-  const uint32_t acc_done = bar0 + 8u * (7 + 2 * ST);
+  auto ds_free = [&](int buf) { return bar0 + 8u * (6 + 2 * ST + buf); };
+  const uint32_t acc_done = bar0 + 8u * (6 + 2 * ST + C::DB);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sp + C::OFF_TMEMPTR);
 
   if (threadIdx.x == 0) {
@@ -393,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(s_free(i), 256);
     }
     mbar_init(ds_full, 256);
-    mbar_init(ds_free, 1);
+    for (int q = 0; q < C::DB; ++q) mbar_init(ds_free(q), 1);
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
@@ -450,12 +471,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < KT / 16; ++k) {
-          const uint64_t da = sdesc_sw128(sb + C::OFF_DS + k * 32, 16, 1024);
+          const uint64_t da = sdesc_sw128(sb + C::OFF_DS + (j % C::DB) * QROWS * 128 + k * 32, 16, 1024);
           const uint64_t kb = sdesc_sw128(base + k * 16 * 128, KT * 128, 1024);
           umma_f16(tmem + C::COL_DQ, da, kb, ID_Q, (j > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(st_free(s));
-        umma_commit(ds_free);
+        umma_commit(ds_free(j % C::DB));
         return true;
       };
       int i = 0;
@@ -515,8 +536,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float p = ex2(sc[c] - lse2);
         dp[c] = p * (dp[c] - delta);
       }
-      if (i > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(ds_free, (i - 1) & 1, kStatusTimeoutSoftmax));
+      if (i >= C::DB) {  // this buffer was last read by the dQ GEMM of iteration i - DB
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(ds_free(i % C::DB), ((i / C::DB) - 1) & 1, kStatusTimeoutSoftmax));
         if (!ok) break;
       }
 #pragma unroll
@@ -525,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint4 w;
         w.x = pack2(dp[c], dp[c + 1], BF16); w.y = pack2(dp[c + 2], dp[c + 3], BF16);
         w.z = pack2(dp[c + 4], dp[c + 5], BF16); w.w = pack2(dp[c + 6], dp[c + 7], BF16);
-        *reinterpret_cast<uint4*>(DS + r * 128 + (((half * (HC / 8) + u) ^ (r & 7)) << 4)) = w;
+        *reinterpret_cast<uint4*>(DS + (i % C::DB) * QROWS * 128 + r * 128 + (((half * (HC / 8) + u) ^ (r & 7)) << 4)) = w;
       }
       fence_proxy_async_smem();
       tc_fence_before();
