@@ -65,13 +65,19 @@ __global__ void append_kernel(V* kp, V* vp, int bs, int row_vecs, const int32_t*
 }
 
 // --------------------------------------------------------------- decode ----
+#ifndef ATTN_PAGED_STAGES
+#define ATTN_PAGED_STAGES 8  // pages in flight per CTA (3 CTAs per SM at page 16)
+#endif
+#ifndef ATTN_PAGED_CHUNK
+#define ATTN_PAGED_CHUNK 2048  // tokens per split
+#endif
 constexpr int NW = 4;                  // consumer warps
 constexpr int kThreads = (NW + 1) * 32;
-constexpr int kChunkTokens = 2048;     // tokens per split
+constexpr int kChunkTokens = ATTN_PAGED_CHUNK;
 
 template <int R>
 struct DecCfg {
-  static constexpr int STAGES = 12;
+  static constexpr int STAGES = ATTN_PAGED_STAGES;
 };
 
 struct DecArgs {
