@@ -11,8 +11,9 @@
 //           dV  += P^T dO, dK  += dS^T Q      (TMEM accumulators)
 //         so dK/dV of a shared KV head are summed over its query heads, the
 //         transpose of the reference's jnp.repeat (attention.py:32-39).
-//   dq:   CTA = 128 q rows of one (batch, query head).  Loops over 64-row kv
-//         tiles:  S = Q K^T, dP = dO V^T, dQ += dS K.
+//   dq:   CTA = 128 q rows of one (batch, query head).  Loops over 128-row kv
+//         tiles:  S = Q K^T, dP = dO V^T, dQ += dS K (S/dP single-buffered in
+//         TMEM and released as soon as the elementwise warps have loaded them).
 //
 // Warp roles in both: warps 0-7 do the elementwise math and the epilogue --
 // warps w and w+4 share TMEM lanes 32*(w%4).. (one row per thread) and split
@@ -34,7 +35,7 @@ namespace bwd {
 #define ATTN_BWD_P_BUFS 1     // dK/dV kernel: P^T/dS^T shared-memory buffers
 #endif
 #ifndef ATTN_BWD_Q_STAGES
-#define ATTN_BWD_Q_STAGES 4   // dQ kernel: K/V tiles in flight
+#define ATTN_BWD_Q_STAGES (ATTN_BWD_DQ_KT == 128 ? 2 : 4)  // dQ kernel: K/V tiles in flight
 #endif
 #ifndef ATTN_BWD_DS_BUFS
 #define ATTN_BWD_DS_BUFS 1    // dQ kernel: dS shared-memory buffers
@@ -43,7 +44,10 @@ constexpr int kThreads = 320;  // warps 0-7 elementwise (two per TMEM lane group
 constexpr int KROWS = 128;  // kv rows per dkdv CTA (MMA M)
 constexpr int QT = 64;      // q rows per dkdv iteration (MMA N)
 constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
-constexpr int KT = 64;      // kv rows per dq iteration (MMA N)
+#ifndef ATTN_BWD_DQ_KT
+#define ATTN_BWD_DQ_KT 128
+#endif
+constexpr int KT = ATTN_BWD_DQ_KT;  // kv rows per dq iteration (MMA N): 64 or 128
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile(
@@ -365,13 +369,16 @@ struct CfgQ {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = Q_BYTES;
   static constexpr int OFF_ST = 2 * Q_BYTES;          // stages: K, V
-  static constexpr int OFF_DS = OFF_ST + ST * 2 * KV_BYTES;  // dS [DB][128 q][64 kv] bf16
-  static constexpr int OFF_BAR = OFF_DS + DB * QROWS * 128;
-  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + DB + 1;
+  static constexpr int DS_BYTES = (KT / 64) * QROWS * 128;   // one dS tile [128 q][KT kv] bf16
+  static constexpr int OFF_DS = OFF_ST + ST * 2 * KV_BYTES;   // dS [DB]
+  static constexpr int OFF_BAR = OFF_DS + DB * DS_BYTES;
+  static constexpr int NSB = (KT == 128) ? 1 : 2;              // TMEM buffers of S and dP
+  static constexpr int NBAR = 1 + 2 * ST + 2 * NSB + 1 + DB + 1;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
+  static_assert(SMEM <= 232448, "dq kernel shared memory");
   static constexpr uint32_t TMEM_COLS = 512;
-  // S[2] at 0/64, dP[2] at 128/192, dQ at 256
+  // S at [0,128), dP at [128,256) (two 64-column buffers each when KT = 64), dQ at 256
   static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DQ = 256;
 };
 
@@ -396,11 +403,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t q_full = bar0;
   auto st_full = [&](int s) { return bar0 + 8u * (1 + s); };
   auto st_free = [&](int s) { return bar0 + 8u * (1 + ST + s); };
+  constexpr int NSB = C::NSB;
   auto s_full = [&](int i) { return bar0 + 8u * (1 + 2 * ST + i); };
-  auto s_free = [&](int i) { return bar0 + 8u * (3 + 2 * ST + i); };
-  const uint32_t ds_full = bar0 + 8u * (5 + 2 * ST);
-  auto ds_free = [&](int buf) { return bar0 + 8u * (6 + 2 * ST + buf); };
-  const uint32_t acc_done = bar0 + 8u * (6 + 2 * ST + C::DB);
+  auto s_free = [&](int i) { return bar0 + 8u * (1 + 2 * ST + NSB + i); };
+  const uint32_t ds_full = bar0 + 8u * (1 + 2 * ST + 2 * NSB);
+  auto ds_free = [&](int buf) { return bar0 + 8u * (2 + 2 * ST + 2 * NSB + buf); };
+  const uint32_t acc_done = bar0 + 8u * (2 + 2 * ST + 2 * NSB + C::DB);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sp + C::OFF_TMEMPTR);
 
   if (threadIdx.x == 0) {
@@ -409,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(st_full(s), 1);
       mbar_init(st_free(s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NSB; ++i) {
       mbar_init(s_full(i), 1);
       mbar_init(s_free(i), 256);
     }
@@ -471,7 +479,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < KT / 16; ++k) {
-          const uint64_t da = sdesc_sw128(sb + C::OFF_DS + (j % C::DB) * QROWS * 128 + k * 32, 16, 1024);
+          const uint64_t da =
+              sdesc_sw128(sb + C::OFF_DS + (j % C::DB) * C::DS_BYTES + (k >> 2) * QROWS * 128 + (k & 3) * 32, 16, 1024);
           const uint64_t kb = sdesc_sw128(base + k * 16 * 128, KT * 128, 1024);
           umma_f16(tmem + C::COL_DQ, da, kb, ID_Q, (j > 0 || k > 0) ? 1u : 0u);
         }
@@ -484,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (state_of(j) == kSkip) continue;
         const int s = i % ST;
         ok = mbar_wait(st_full(s), (i / ST) & 1, kStatusTimeoutMma) &&
-             mbar_wait(s_free(i & 1), ((i >> 1) & 1) ^ 1, kStatusTimeoutMma);
+             mbar_wait(s_free(i % NSB), ((i / NSB) & 1) ^ 1, kStatusTimeoutMma);
         if (!ok) break;
         tc_fence_after();
         const uint32_t base = sb + C::OFF_ST + s * 2 * C::KV_BYTES;
@@ -495,10 +504,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t oa = sdesc_sw128(sb + C::OFF_DO + (k >> 2) * QROWS * 128 + off, 16, 1024);
           const uint64_t kb = sdesc_sw128(base + (k >> 2) * KT * 128 + off, 16, 1024);
           const uint64_t vb = sdesc_sw128(base + C::KV_BYTES + (k >> 2) * KT * 128 + off, 16, 1024);
-          umma_f16(tmem + C::COL_S + (i & 1) * KT, qa, kb, ID_S, k > 0 ? 1u : 0u);
-          umma_f16(tmem + C::COL_DP + (i & 1) * KT, oa, vb, ID_S, k > 0 ? 1u : 0u);
+          umma_f16(tmem + C::COL_S + (i % NSB) * KT, qa, kb, ID_S, k > 0 ? 1u : 0u);
+          umma_f16(tmem + C::COL_DP + (i % NSB) * KT, oa, vb, ID_S, k > 0 ? 1u : 0u);
         }
-        umma_commit(s_full(i & 1));
+        umma_commit(s_full(i % NSB));
         if (i > 0) ok = issue_dq(i - 1);
         ++i;
       }
@@ -507,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 8) {
     const int r = threadIdx.x & 127;  // q row within the tile == TMEM lane
-    const int half = warp >> 2;       // columns [32*half, 32*half + 32) of each kv tile
+    const int half = warp >> 2;       // columns [KT/2*half, KT/2*(half+1)) of each kv tile
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const bool row_ok = q0 + r < a.Sq;
     const long long ridx = ((long long)b * a.Hq + hq) * a.Sq_pad + q0 + r;
@@ -518,36 +527,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = j_lo; j < j_hi; ++j) {
       const int st = state_of(j);
       if (st == kSkip) continue;
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, kStatusTimeoutSoftmax));
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full(i % NSB), (i / NSB) & 1, kStatusTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-      constexpr int HC = KT / 2;  // columns per thread
-      float sc[HC], dp[HC];
-      tmem_ld32(tmem + lane_base + C::COL_S + (i & 1) * KT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(sc));
-      tmem_ld32(tmem + lane_base + C::COL_DP + (i & 1) * KT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(dp));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(s_free(i & 1));
-      const int c0 = j * KT + half * HC;
-      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, c0, max(0, min(HC, a.Skv - c0)), false);
-      transform_row<HC>(sc, rc, st == kPartial);
-#pragma unroll
-      for (int c = 0; c < HC; ++c) {
-        const float p = ex2(sc[c] - lse2);
-        dp[c] = p * (dp[c] - delta);
-      }
-      if (i >= C::DB) {  // this buffer was last read by the dQ GEMM of iteration i - DB
+      constexpr int HC = KT / 2;  // columns per thread, processed 32 at a time
+      if (i >= C::DB) {  // this dS buffer was last read by the dQ GEMM of iteration i - DB
         ok = __all_sync(0xffffffffu,
                         mbar_wait(ds_free(i % C::DB), ((i / C::DB) - 1) & 1, kStatusTimeoutSoftmax));
         if (!ok) break;
       }
+      uint8_t* dsb = DS + (i % C::DB) * C::DS_BYTES;
+#pragma unroll 1
+      for (int cc = 0; cc < HC / 32; ++cc) {
+        float sc[32], dp[32];
+        tmem_ld32(tmem + lane_base + C::COL_S + (i % NSB) * KT + half * HC + cc * 32,
+                  *reinterpret_cast<uint32_t(*)[32]>(sc));
+        tmem_ld32(tmem + lane_base + C::COL_DP + (i % NSB) * KT + half * HC + cc * 32,
+                  *reinterpret_cast<uint32_t(*)[32]>(dp));
+        tmem_wait_ld();
+        if (cc == HC / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(s_free(i % NSB));
+        }
+        const int c0 = j * KT + half * HC + cc * 32;
+        const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, c0, max(0, min(32, a.Skv - c0)), false);
+        transform_row<32>(sc, rc, st == kPartial);
 #pragma unroll
-      for (int u = 0; u < HC / 8; ++u) {
-        const int c = u * 8;
-        uint4 w;
-        w.x = pack2(dp[c], dp[c + 1], BF16); w.y = pack2(dp[c + 2], dp[c + 3], BF16);
-        w.z = pack2(dp[c + 4], dp[c + 5], BF16); w.w = pack2(dp[c + 6], dp[c + 7], BF16);
-        *reinterpret_cast<uint4*>(DS + (i % C::DB) * QROWS * 128 + r * 128 + (((half * (HC / 8) + u) ^ (r & 7)) << 4)) = w;
+        for (int c = 0; c < 32; ++c) {
+          const float p = ex2(sc[c] - lse2);
+          dp[c] = p * (dp[c] - delta);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = u * 8, ca = half * HC + cc * 32 + c;  // column within the KT-wide tile
+          uint4 w;
+          w.x = pack2(dp[c], dp[c + 1], BF16); w.y = pack2(dp[c + 2], dp[c + 3], BF16);
+          w.z = pack2(dp[c + 4], dp[c + 5], BF16); w.w = pack2(dp[c + 6], dp[c + 7], BF16);
+          *reinterpret_cast<uint4*>(dsb + (ca >> 6) * QROWS * 128 + r * 128 + ((((ca & 63) >> 3) ^ (r & 7)) << 4)) = w;
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
