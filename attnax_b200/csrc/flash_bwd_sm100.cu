@@ -7,7 +7,8 @@
 //
 //   dkdv: CTA = 128 kv rows of one (batch, kv head).  Loops over every query
 //         head of the GQA group and every 64-row q tile the mask keeps:
-//           S^T  = K Q^T,  dP^T = V dO^T      (TMEM, double buffered)
+//           S^T  = K Q^T,  dP^T = V dO^T      (K and V read from TMEM, where the
+//                                              CTA stores them once; S^T/dP^T in TMEM)
 //           dV  += P^T dO, dK  += dS^T Q      (TMEM accumulators)
 //         so dK/dV of a shared KV head are summed over its query heads, the
 //         transpose of the reference's jnp.repeat (attention.py:32-39).
@@ -44,6 +45,9 @@ constexpr int kThreads = 320;  // warps 0-7 elementwise (two per TMEM lane group
 constexpr int KROWS = 128;  // kv rows per dkdv CTA (MMA M)
 constexpr int QT = 64;      // q rows per dkdv iteration (MMA N)
 constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
+#ifndef ATTN_BWD_KV_TMEM
+#define ATTN_BWD_KV_TMEM 1    // dK/dV kernel: K and V copied once into TMEM as the A operand of S^T, dP^T
+#endif
 #ifndef ATTN_BWD_DQ_KT
 #define ATTN_BWD_DQ_KT 128
 #endif
@@ -100,12 +104,18 @@ struct CfgKV {
   static constexpr int OFF_P = OFF_ST + ST * STAGE;           // P^T  [PB][128 kv][64 q] bf16
   static constexpr int OFF_DS = OFF_P + PB * KROWS * 128;     // dS^T [PB][128 kv][64 q] bf16
   static constexpr int OFF_BAR = OFF_DS + PB * KROWS * 128;
-  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + PB + 1;
+  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + PB + 1 + 1;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   // TMEM columns: S^T[2] at 0/64, dP^T[2] at 128/192, dV at 256, dK at 256 + D
-  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 256 + D;
+  // TMEM columns.  With K/V in TMEM: K [0, D/2), V [D/2, D) as bf16 pairs, S^T at 128 and
+  // dP^T at 192 (single buffers); otherwise S^T [2] at 0/64 and dP^T [2] at 128/192.
+  static constexpr bool KV_TMEM = ATTN_BWD_KV_TMEM != 0;
+  static constexpr int NSB = KV_TMEM ? 1 : 2;
+  static constexpr uint32_t COL_K = 0, COL_V = D / 2;
+  static constexpr uint32_t COL_S = KV_TMEM ? 128 : 0, COL_DP = KV_TMEM ? 192 : 128;
+  static constexpr uint32_t COL_DV = 256, COL_DK = 256 + D;
 };
 
 template <int D, bool BF16>
@@ -132,6 +142,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t p_full = bar0 + 8u * (5 + 2 * ST);
   auto p_free = [&](int buf) { return bar0 + 8u * (6 + 2 * ST + buf); };
   const uint32_t acc_done = bar0 + 8u * (6 + 2 * ST + C::PB);
+  const uint32_t kv_tmem = bar0 + 8u * (7 + 2 * ST + C::PB);  // K/V rows stored into TMEM
+  constexpr int NSB = C::NSB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sp + C::OFF_TMEMPTR);
 
   if (threadIdx.x == 0) {
@@ -140,13 +152,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(st_full(s), 1);
       mbar_init(st_free(s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NSB; ++i) {
       mbar_init(s_full(i), 1);
       mbar_init(s_free(i), 256);
     }
     mbar_init(p_full, 256);
     for (int q = 0; q < C::PB; ++q) mbar_init(p_free(q), 1);
     mbar_init(acc_done, 1);
+    mbar_init(kv_tmem, 256);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -204,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t ID_S = idesc_f16(128, QT, FMT, 0, 0);
       constexpr uint32_t ID_G = idesc_f16(128, D, FMT, 0, 1);
       bool ok = mbar_wait(kv_full, 0, kStatusTimeoutMma);
+      if (C::KV_TMEM) ok = ok && mbar_wait(kv_tmem, 0, kStatusTimeoutMma);
       auto issue_grads = [&](int j) -> bool {
         const int s = j % ST;
         const uint32_t base = sb + C::OFF_ST + s * C::STAGE;
@@ -227,21 +241,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (state_of(it) == kSkip) continue;
         const int s = i % ST;
         ok = mbar_wait(st_full(s), (i / ST) & 1, kStatusTimeoutMma) &&
-             mbar_wait(s_free(i & 1), ((i >> 1) & 1) ^ 1, kStatusTimeoutMma);
+             mbar_wait(s_free(i % NSB), ((i / NSB) & 1) ^ 1, kStatusTimeoutMma);
         if (!ok) break;
         tc_fence_after();
         const uint32_t base = sb + C::OFF_ST + s * C::STAGE;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t off = (k & 3) * 32;
-          const uint64_t ka = sdesc_sw128(sb + C::OFF_K + (k >> 2) * KROWS * 128 + off, 16, 1024);
-          const uint64_t va = sdesc_sw128(sb + C::OFF_V + (k >> 2) * KROWS * 128 + off, 16, 1024);
           const uint64_t qb = sdesc_sw128(base + (k >> 2) * QT * 128 + off, 16, 1024);
           const uint64_t db = sdesc_sw128(base + C::QD_BYTES + (k >> 2) * QT * 128 + off, 16, 1024);
-          umma_f16(tmem + C::COL_S + (i & 1) * QT, ka, qb, ID_S, k > 0 ? 1u : 0u);
-          umma_f16(tmem + C::COL_DP + (i & 1) * QT, va, db, ID_S, k > 0 ? 1u : 0u);
+          if (C::KV_TMEM) {
+            umma_f16_ts(tmem + C::COL_S, tmem + C::COL_K + k * 8, qb, ID_S, k > 0 ? 1u : 0u);
+            umma_f16_ts(tmem + C::COL_DP, tmem + C::COL_V + k * 8, db, ID_S, k > 0 ? 1u : 0u);
+          } else {
+            const uint64_t ka = sdesc_sw128(sb + C::OFF_K + (k >> 2) * KROWS * 128 + off, 16, 1024);
+            const uint64_t va = sdesc_sw128(sb + C::OFF_V + (k >> 2) * KROWS * 128 + off, 16, 1024);
+            umma_f16(tmem + C::COL_S + (i % NSB) * QT, ka, qb, ID_S, k > 0 ? 1u : 0u);
+            umma_f16(tmem + C::COL_DP + (i % NSB) * QT, va, db, ID_S, k > 0 ? 1u : 0u);
+          }
         }
-        umma_commit(s_full(i & 1));
+        umma_commit(s_full(i % NSB));
         if (i > 0) ok = issue_grads(i - 1);
         ++i;
       }
@@ -256,22 +275,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* DST = sp + C::OFF_DS;
     int i = 0;
     bool ok = true;
+    if (C::KV_TMEM) {
+      // Warps 0-3 store their K row, warps 4-7 their V row, into TMEM as bf16 pairs.
+      ok = __all_sync(0xffffffffu, mbar_wait(kv_full, 0, kStatusTimeoutSoftmax));
+      if (ok) {
+        const uint8_t* src = sp + (half ? C::OFF_V : C::OFF_K);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t w[32];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint4 v = *reinterpret_cast<const uint4*>(src + c * KROWS * 128 + r * 128 + ((u ^ (r & 7)) << 4));
+            w[u * 4 + 0] = v.x; w[u * 4 + 1] = v.y; w[u * 4 + 2] = v.z; w[u * 4 + 3] = v.w;
+          }
+          tmem_st32(tmem + lane_base + (half ? C::COL_V : C::COL_K) + c * 32, w);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(kv_tmem);
+    }
     for (int it = 0; it < iters; ++it) {
       const int st = state_of(it);
       if (st == kSkip) continue;
       const int g = it / ntiles, qt = t_lo + it % ntiles;
       const int hq = hkv * a.group + g, q0 = qt * QT;
       const int s = i % ST;
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full(i & 1), (i >> 1) & 1, kStatusTimeoutSoftmax));
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full(i % NSB), (i / NSB) & 1, kStatusTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
       constexpr int HC = QT / 2;  // columns per thread
       float sc[HC], dp[HC];
-      tmem_ld32(tmem + lane_base + C::COL_S + (i & 1) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(sc));
-      tmem_ld32(tmem + lane_base + C::COL_DP + (i & 1) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(dp));
+      tmem_ld32(tmem + lane_base + C::COL_S + (i % NSB) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(sc));
+      tmem_ld32(tmem + lane_base + C::COL_DP + (i % NSB) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(dp));
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(s_free(i & 1));
+      mbar_arrive(s_free(i % NSB));
       const int c0 = q0 + half * HC;
       const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, k0 + r, c0, max(0, min(HC, a.Sq - c0)), true);
       transform_row<HC>(sc, rc, st == kPartial || k0 + r >= a.Skv);
