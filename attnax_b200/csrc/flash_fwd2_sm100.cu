@@ -15,7 +15,9 @@
 //   * tensor-core order S_A(j), S_B(j), PV_A(j), S_A(j+1), PV_B(j), S_B(j+1),
 //     so each softmax overlaps two GEMMs of the other tile;
 //   * O is rescaled only when a row maximum grows by more than 2^8 (the
-//     stale maximum keeps P <= 256, exact after the final 1/l);
+//     stale maximum keeps P <= 256, exact after the final 1/l); kv tiles run
+//     from the diagonal downwards, so under ALiBi the first tile already
+//     holds the largest bias and rescales become rare;
 //   * one exponential in ATTN_FWD2_POLY_EVERY uses a cubic polynomial on the
 //     FMA pipe (2^x = 2^n * p(f), n = round(x), |f| <= 1/2, coefficients
 //     fitted for this kernel) to take load off the MUFU pipe;
@@ -41,6 +43,9 @@ constexpr float kRescaleThreshold = 8.f;  // log2 units
 #endif
 #ifndef ATTN_FWD2_MAX3
 #define ATTN_FWD2_MAX3 0  // three-input max in the row-max tree
+#endif
+#ifndef ATTN_FWD2_REVERSE
+#define ATTN_FWD2_REVERSE 1  // kv tiles from the diagonal down: the first tile holds the row maximum under ALiBi
 #endif
 #ifndef ATTN_FWD2_POLY_EVERY
 #define ATTN_FWD2_POLY_EVERY 0  // one exponential in this many uses the FMA-pipe polynomial (0: none)
@@ -149,6 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int j_lo = act[1] ? min(jl[0], jl[1]) : jl[0];
   const int j_hi = act[1] ? max(jh[0], jh[1]) : jh[0];
+  // kv tile visited at position t of the loop (all three roles use the same order).
+  auto kv_tile = [&](int t) { return ATTN_FWD2_REVERSE ? j_hi - 1 - t : j_lo + t; };
+  const int n_tiles = j_hi - j_lo;
   auto state_of = [&](int x, int j) {
     if (!act[x] || j < jl[x] || j >= jh[x]) return (int)kSkip;
     return tile_state(a.mask, a.doc_q_tiles, a.doc_kv_tiles, a.nq_doc, a.nk_doc, b, q0[x], q1[x], j * BN,
@@ -168,7 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < C::KCH; ++c)
           tma_load_4d(sb + C::OFF_Q + x * C::Q_BYTES + c * BM * 128, &tm_q, q_full, c * 64, q0[x], hq, b);
       int n = 0;
-      for (int j = j_lo; j < j_hi; ++j) {
+      for (int t = 0; t < n_tiles; ++t) {
+        const int j = kv_tile(t);
         if (state_of(0, j) == kSkip && state_of(1, j) == kSkip) continue;
         const int s = n % S;
         if (!mbar_wait(kv_empty(s), ((n / S) & 1) ^ 1, kStatusTimeoutLoad)) break;
@@ -222,7 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++pv[x];
         return true;
       };
-      for (int j = j_lo; ok && j < j_hi; ++j) {
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int j = kv_tile(t);
         const bool ax = state_of(0, j) != kSkip, bx = state_of(1, j) != kSkip;
         if (!ax && !bx) continue;
         const int s = n % S;
@@ -275,7 +285,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int band_lo = a.mask.has_band ? clamp_i32(a.mask.band_lo) : -(1 << 30);
     const int band_hi = a.mask.has_band ? clamp_i32(a.mask.band_hi) : (1 << 30);
     const long long pref = a.mask.prefix_len ? (long long)a.mask.prefix_len[b] : -1;
-    for (int j = j_lo; j < j_hi; ++j) {
+    for (int t = 0; t < n_tiles; ++t) {
+      const int j = kv_tile(t);
       const int st = state_of(x, j);
       if (st == kSkip) continue;
       ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), i & 1, kStatusTimeoutSoftmax));
