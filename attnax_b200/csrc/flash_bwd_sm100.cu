@@ -48,6 +48,9 @@ constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
 #ifndef ATTN_BWD_KV_TMEM
 #define ATTN_BWD_KV_TMEM 1    // dK/dV kernel: K and V copied once into TMEM as the A operand of S^T, dP^T
 #endif
+#ifndef ATTN_BWD_FAST_FULL
+#define ATTN_BWD_FAST_FULL 1  // full tiles: hoisted row constants, linear ALiBi, packed f32x2 math
+#endif
 #ifndef ATTN_BWD_DQ_KT
 #define ATTN_BWD_DQ_KT 128
 #endif
@@ -103,7 +106,8 @@ struct CfgKV {
   static constexpr int OFF_ST = 2 * KV_BYTES;                 // stages: Q, dO, lse2, delta
   static constexpr int OFF_P = OFF_ST + ST * STAGE;           // P^T  [PB][128 kv][64 q] bf16
   static constexpr int OFF_DS = OFF_P + PB * KROWS * 128;     // dS^T [PB][128 kv][64 q] bf16
-  static constexpr int OFF_BAR = OFF_DS + PB * KROWS * 128;
+  static constexpr int OFF_COLV = OFF_DS + PB * KROWS * 128;  // per elementwise warp: 32 column terms
+  static constexpr int OFF_BAR = OFF_COLV + 8 * 32 * 4;
   static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + PB + 1 + 1;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
@@ -273,6 +277,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     uint8_t* PT = sp + C::OFF_P;
     uint8_t* DST = sp + C::OFF_DS;
+    float* colv = reinterpret_cast<float*>(sp + C::OFF_COLV) + warp * 32;
+    // Full tiles: with no ALiBi, or ALiBi under a causal band (every kept
+    // score has q >= kv), t = s*sl2 - slope*(d0 + c) - lse2[c] with
+    // d0 = q(column 0) - kv(row); the column part -slope*c - lse2[c] is
+    // computed once per warp and shared through shared memory.
+    const bool fast_mask = ATTN_BWD_FAST_FULL && (!a.mask.alibi_slopes || (a.mask.has_band && a.mask.band_lo >= 0));
+    const long long kg_row = a.mask.kv_offset + k0 + r;
+    const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2);
     int i = 0;
     bool ok = true;
     if (C::KV_TMEM) {
@@ -312,21 +324,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(s_free(i % NSB));
       const int c0 = q0 + half * HC;
-      const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, k0 + r, c0, max(0, min(HC, a.Sq - c0)), true);
-      transform_row<HC>(sc, rc, st == kPartial || k0 + r >= a.Skv);
       const float* sl = reinterpret_cast<const float*>(sp + C::OFF_ST + s * C::STAGE + 2 * C::QD_BYTES) + half * HC;
       const float* sd = sl + QT;
-      const bool row_ok = k0 + r < a.Skv;
+      if (st == kFull && fast_mask) {
+        // (a full tile has all KROWS kv rows inside the sequence; q columns
+        // past the end carry lse2 = +inf and delta = 0, so P = dS = 0 there)
+        static_assert(HC == 32, "one column term per lane");
+        const float slope = a.mask.alibi_slopes ? __ldg(a.mask.alibi_slopes + hq) * kLog2e : 0.f;
+        __syncwarp();
+        colv[lane] = fmaf(-slope, (float)lane, -sl[lane]);
+        __syncwarp();
+        const float base = -slope * (float)clamp_i32(a.mask.q_offset + c0 - kg_row);
+        const unsigned long long base2 = f2_pack(base, base);
 #pragma unroll
-      for (int c = 0; c < HC; c += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(sl + c);
-        const float4 d4 = *reinterpret_cast<const float4*>(sd + c);
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+        for (int c = 0; c < HC; c += 4) {
+          const float4 v4 = *reinterpret_cast<const float4*>(colv + c);
+          const float4 d4 = *reinterpret_cast<const float4*>(sd + c);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p = row_ok ? ex2(sc[c + e] - lv[e]) : 0.f;
-          sc[c + e] = p;
-          dp[c + e] = p * (dp[c + e] - dv4[e]);
+          for (int e = 0; e < 4; e += 2) {
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(sc[c + e], sc[c + e + 1]), sl2x2,
+                             f2_add(base2, e ? f2_pack(v4.z, v4.w) : f2_pack(v4.x, v4.y))), x0, x1);
+            const unsigned long long p2 = f2_pack(ex2(x0), ex2(x1));
+            const unsigned long long g2 = f2_mul(p2, f2_sub(f2_pack(dp[c + e], dp[c + e + 1]),
+                                                            e ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y)));
+            f2_unpack(p2, sc[c + e], sc[c + e + 1]);
+            f2_unpack(g2, dp[c + e], dp[c + e + 1]);
+          }
+        }
+      } else {
+        const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, k0 + r, c0, max(0, min(HC, a.Sq - c0)), true);
+        transform_row<HC>(sc, rc, st == kPartial || k0 + r >= a.Skv);
+        const bool row_ok = k0 + r < a.Skv;
+#pragma unroll
+        for (int c = 0; c < HC; c += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(sl + c);
+          const float4 d4 = *reinterpret_cast<const float4*>(sd + c);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p = row_ok ? ex2(sc[c + e] - lv[e]) : 0.f;
+            sc[c + e] = p;
+            dp[c + e] = p * (dp[c + e] - dv4[e]);
+          }
         }
       }
       if (i >= C::PB) {  // this buffer was last read by the gradient GEMMs of iteration i - PB
@@ -561,6 +601,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const long long ridx = ((long long)b * a.Hq + hq) * a.Sq_pad + q0 + r;
     const float lse2 = a.lse2[ridx], delta = a.delta[ridx];
     uint8_t* DS = sp + C::OFF_DS;
+    // Full tiles: t = s*sl2 - slope*(d0 - c) - lse2 (d0 = q - kv(column 0) >= c
+    // under a causal band), i.e. a per-row constant plus slope*c.
+    const float slope_l2 = a.mask.alibi_slopes ? a.mask.alibi_slopes[hq] * kLog2e : 0.f;
+    const bool fast_mask = ATTN_BWD_FAST_FULL && (!a.mask.alibi_slopes || (a.mask.has_band && a.mask.band_lo >= 0));
+    const long long qg_row = a.mask.q_offset + q0 + r;
+    const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2), delta2 = f2_pack(delta, delta);
+    const unsigned long long step2 = f2_pack(8.f * slope_l2, 8.f * slope_l2);
     int i = 0;
     bool ok = true;
     for (int j = j_lo; j < j_hi; ++j) {
@@ -589,12 +636,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(s_free(i % NSB));
         }
         const int c0 = j * KT + half * HC + cc * 32;
-        const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, c0, max(0, min(32, a.Skv - c0)), false);
-        transform_row<32>(sc, rc, st == kPartial);
+        if (st == kFull && fast_mask) {
+          const float rowc = -slope_l2 * (float)clamp_i32(qg_row - (a.mask.kv_offset + c0)) - lse2;
+          unsigned long long addv[4];  // rowc + slope*c for the column pairs, 4 independent chains
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p = ex2(sc[c] - lse2);
-          dp[c] = p * (dp[c] - delta);
+          for (int q = 0; q < 4; ++q)
+            addv[q] = f2_pack(fmaf(slope_l2, (float)(2 * q), rowc), fmaf(slope_l2, (float)(2 * q + 1), rowc));
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const int q = (c >> 1) & 3;
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(sc[c], sc[c + 1]), sl2x2, addv[q]), x0, x1);
+            addv[q] = f2_add(addv[q], step2);
+            const unsigned long long p2 = f2_pack(ex2(x0), ex2(x1));
+            f2_unpack(f2_mul(p2, f2_sub(f2_pack(dp[c], dp[c + 1]), delta2)), dp[c], dp[c + 1]);
+          }
+        } else {
+          const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, c0, max(0, min(32, a.Skv - c0)), false);
+          transform_row<32>(sc, rc, st == kPartial);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float p = ex2(sc[c] - lse2);
+            dp[c] = p * (dp[c] - delta);
+          }
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {

@@ -39,6 +39,12 @@ def pair(name, H, S, B):
     if name == "window_alibi":
         return (ax.compose_score_mods(ax.sliding_window_mod(90), ax.alibi_mod(H)),
                 O.compose_score_mods(O.sliding_window_mod(90), O.alibi_mod(H)))
+    if name == "causal_alibi":
+        return (ax.compose_score_mods(ax.causal_mod(), ax.alibi_mod(H)),
+                O.compose_score_mods(O.causal_mod(), O.alibi_mod(H)))
+    if name == "window_alibi_wide":
+        return (ax.compose_score_mods(ax.sliding_window_mod(400), ax.alibi_mod(H)),
+                O.compose_score_mods(O.sliding_window_mod(400), O.alibi_mod(H)))
     if name == "prefix":
         pref = np.array([37, 200][:B] + [5] * max(0, B - 2), np.int32)
         return ax.prefix_lm_mod(pref), O.prefix_lm_mod(pref)
@@ -173,6 +179,24 @@ def test_backward(dtype, D, mod):
             assert_bf16_close(npy(got), w, f"{mod} {name}", scale_with_max=True)
         else:
             assert_fp32_close(npy(got), w, f"{mod} {name}", atol=2e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("mod", ["none", "causal_alibi", "window_alibi_wide"])
+def test_backward_full_tiles(dtype, mod):
+    """Long enough that whole 128x64 / 128x128 tiles lie inside the band, so
+    the full-tile path (linear ALiBi, packed arithmetic) runs next to the
+    boundary-tile path; ragged length; GQA with per-head slopes."""
+    rng = np.random.default_rng(8)
+    B, Hq, Hkv, S, D = 1, 4, 2, 700, 128
+    q, k, v, do = (randn(rng, (B, h, S, D), True) for h in (Hq, Hkv, Hkv, Hq))
+    m_ax, m_o = pair(mod, Hq, S, B)
+    tq, tk, tv = T(q, dtype, True), T(k, dtype, True), T(v, dtype, True)
+    out = ax.flash_attention(tq, tk, tv, score_mod=m_ax)
+    out.backward(T(do, dtype))
+    want = O.gqa_attention_bwd(q, k, v, do, score_mod=m_o)
+    for name, got, w in zip(("dq", "dk", "dv"), (tq.grad, tk.grad, tv.grad), want):
+        assert_bf16_close(npy(got), w, f"{mod} {name}", scale_with_max=True)
 
 
 def test_backward_fully_masked_rows():
