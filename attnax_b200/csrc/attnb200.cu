@@ -399,8 +399,35 @@ static bool bwd_tc_ok(const attn_bwd_params_t* p) {
 
 static int bwd_seq_pad(const attn_bwd_params_t* p) { return (p->seq_q + 127) / 128 * 128; }
 
+static bool bwd_fused_dq(const attn_bwd_params_t* p) { return ATTN_BWD_FUSED_DQ && p->head_dim == 128; }
+
+struct BwdWorkspace {
+  size_t lse2 = 0, dq_acc = 0, total = 0;  // delta at offset 0
+};
+
+static BwdWorkspace bwd_workspace_layout(const attn_bwd_params_t* p) {
+  BwdWorkspace w;
+  const bool tc = bwd_tc_ok(p);
+  const size_t rows = (size_t)p->batch * p->num_heads_q * (tc ? bwd_seq_pad(p) : p->seq_q);
+  w.lse2 = align256(rows * sizeof(float));
+  w.dq_acc = 2 * w.lse2;
+  w.total = w.dq_acc + ((tc && bwd_fused_dq(p)) ? align256(rows * p->head_dim * sizeof(float)) : 0);
+  return w;
+}
+
+// Sets the kernel's dynamic shared-memory limit once per device.
+template <typename K>
+static bool smem_attr_once(K kernel, int bytes, int* cached_dev) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (*cached_dev == dev) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  *cached_dev = dev;
+  return true;
+}
+
 template <int D, bool BF16>
-static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse2, cudaStream_t st) {
+static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse2, float* dq_acc, cudaStream_t st) {
   using namespace bwd;
   const int Sq_pad = bwd_seq_pad(p);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -413,7 +440,7 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
   a.Sq_pad = Sq_pad; a.group = p->num_heads_q / p->num_heads_kv;
   a.sl2 = p->softmax_scale * kLog2e; a.scale = p->softmax_scale;
   a.lse2 = lse2; a.delta = delta;
-  a.dq = p->dq; a.dk = p->dk; a.dv = p->dv;
+  a.dq = p->dq; a.dk = p->dk; a.dv = p->dv; a.dq_acc = dq_acc;
   for (int i = 0; i < 3; ++i) {
     a.dq_s[i] = p->dq_strides[i]; a.dk_s[i] = p->dk_strides[i]; a.dv_s[i] = p->dv_strides[i];
   }
@@ -429,22 +456,28 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
       !make_tmap(&k64, p->dtype, p->k, B, Hkv, Skv, D, p->k_strides, KT) ||
       !make_tmap(&v64, p->dtype, p->v, B, Hkv, Skv, D, p->v_strides, KT))
     return ATTN_ERR_INVALID;
-  auto kkv = dkdv_kernel<D, BF16>;
-  auto kq = dq_kernel<D, BF16>;
+  const dim3 grid_kv((Skv + KROWS - 1) / KROWS, Hkv, B);
+  if constexpr (D == 128) {
+    if (bwd_fused_dq(p)) {
+      // dQ accumulated in fp32 by the dK/dV kernel, then scaled and converted.
+      static int attr_dev_f = -1;
+      auto kf = dkdv_kernel<D, BF16, true>;
+      if (!smem_attr_once(kf, CfgKV<D, true>::SMEM, &attr_dev_f)) return ATTN_ERR_CUDA;
+      if (cudaMemsetAsync(dq_acc, 0, (size_t)B * Hq * Sq_pad * D * sizeof(float), st) != cudaSuccess)
+        return ATTN_ERR_CUDA;
+      kf<<<grid_kv, kThreads, CfgKV<D, true>::SMEM, st>>>(q64, k128, v128, do64, a);
+      dq_convert_kernel<T><<<dim3((Sq + 7) / 8, Hq, B), 256, 0, st>>>(
+          dq_acc, reinterpret_cast<T*>(p->dq), p->dq_strides[0], p->dq_strides[1], p->dq_strides[2], Hq, Sq,
+          Sq_pad, D, p->softmax_scale);
+      return launch_status(3);
+    }
+  }
   static int attr_dev_kv = -1, attr_dev_q = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_dev_kv != dev) {
-    if (cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgKV<D>::SMEM) != cudaSuccess)
-      return ATTN_ERR_CUDA;
-    attr_dev_kv = dev;
-  }
-  if (attr_dev_q != dev) {
-    if (cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgQ<D>::SMEM) != cudaSuccess)
-      return ATTN_ERR_CUDA;
-    attr_dev_q = dev;
-  }
-  kkv<<<dim3((Skv + KROWS - 1) / KROWS, Hkv, B), kThreads, CfgKV<D>::SMEM, st>>>(q64, k128, v128, do64, a);
+  auto kkv = dkdv_kernel<D, BF16, false>;
+  auto kq = dq_kernel<D, BF16>;
+  if (!smem_attr_once(kkv, CfgKV<D, false>::SMEM, &attr_dev_kv) || !smem_attr_once(kq, CfgQ<D>::SMEM, &attr_dev_q))
+    return ATTN_ERR_CUDA;
+  kkv<<<grid_kv, kThreads, CfgKV<D, false>::SMEM, st>>>(q64, k128, v128, do64, a);
   kq<<<dim3((Sq + QROWS - 1) / QROWS, Hq, B), kThreads, CfgQ<D>::SMEM, st>>>(q128, k64, v64, do128, a);
   return launch_status(3);
 }
@@ -455,8 +488,7 @@ extern "C" {
 
 size_t attn_bwd_workspace_size(const attn_bwd_params_t* p) {
   if (!p) return 0;
-  const size_t rows = (size_t)p->batch * p->num_heads_q * (bwd_tc_ok(p) ? bwd_seq_pad(p) : p->seq_q);
-  return 2 * align256(rows * sizeof(float));
+  return bwd_workspace_layout(p).total;
 }
 
 int attn_bwd(const attn_bwd_params_t* p, void* stream) {
@@ -471,8 +503,10 @@ int attn_bwd(const attn_bwd_params_t* p, void* stream) {
   const size_t need = attn_bwd_workspace_size(p);
   if (!p->workspace || p->workspace_bytes < need) return ATTN_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const BwdWorkspace wl = bwd_workspace_layout(p);
   float* delta = reinterpret_cast<float*>(p->workspace);
-  float* lse2 = reinterpret_cast<float*>(reinterpret_cast<char*>(p->workspace) + need / 2);
+  float* lse2 = reinterpret_cast<float*>(reinterpret_cast<char*>(p->workspace) + wl.lse2);
+  float* dq_acc = reinterpret_cast<float*>(reinterpret_cast<char*>(p->workspace) + wl.dq_acc);
   const int grp = p->num_heads_q / p->num_heads_kv;
 
   simt::BwdArgs a;
@@ -491,9 +525,11 @@ int attn_bwd(const attn_bwd_params_t* p, void* stream) {
     int rc;
     const bool bf = p->dtype == ATTN_BF16;
     if (p->head_dim == 128)
-      rc = bf ? launch_sm100_bwd<128, true>(p, delta, lse2, st) : launch_sm100_bwd<128, false>(p, delta, lse2, st);
+      rc = bf ? launch_sm100_bwd<128, true>(p, delta, lse2, dq_acc, st)
+              : launch_sm100_bwd<128, false>(p, delta, lse2, dq_acc, st);
     else
-      rc = bf ? launch_sm100_bwd<64, true>(p, delta, lse2, st) : launch_sm100_bwd<64, false>(p, delta, lse2, st);
+      rc = bf ? launch_sm100_bwd<64, true>(p, delta, lse2, dq_acc, st)
+              : launch_sm100_bwd<64, false>(p, delta, lse2, dq_acc, st);
     if (rc != ATTN_OK || !p->fix_masked_rows) return rc;
     auto fix = [&](auto tag) {
       using T = decltype(tag);

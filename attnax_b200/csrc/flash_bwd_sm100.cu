@@ -3,7 +3,8 @@
 // standard_attention (attnax/kernels/attention.py:54-71).  With
 // P = softmax(S), dV = P^T dO, dS = P * (dO V^T - rowsum(dO * O)),
 // dQ = scale * dS K and dK = scale * dS^T Q; P is recomputed from the LSE of
-// the forward.  Two deterministic kernels (no atomics):
+// the forward.  Head dim 128 runs one kernel (dkdv with fused dQ); other
+// head dims run two deterministic kernels (dkdv, then dq):
 //
 //   dkdv: CTA = 128 kv rows of one (batch, kv head).  Loops over every query
 //         head of the GQA group and every 64-row q tile the mask keeps:
@@ -12,6 +13,12 @@
 //           dV  += P^T dO, dK  += dS^T Q      (TMEM accumulators)
 //         so dK/dV of a shared KV head are summed over its query heads, the
 //         transpose of the reference's jnp.repeat (attention.py:32-39).
+//         Fused dQ (D = 128): also dQ^T = K^T dS^T per tile (M = head dim,
+//         N = 64 q, two TMEM buffers); the elementwise warps stage it as
+//         [64 q][D] fp32 in shared memory and one thread adds the 32 KB into
+//         an fp32 dQ accumulator with a bulk reduction (L2 performs the
+//         adds; summation order across kv tiles is not fixed).  K and V stay
+//         in shared memory there, S^T/dP^T are single-buffered.
 //   dq:   CTA = 128 q rows of one (batch, query head).  Loops over 128-row kv
 //         tiles:  S = Q K^T, dP = dO V^T, dQ += dS K (S/dP single-buffered in
 //         TMEM and released as soon as the elementwise warps have loaded them).
@@ -51,6 +58,9 @@ constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
 #ifndef ATTN_BWD_FAST_FULL
 #define ATTN_BWD_FAST_FULL 1  // full tiles: hoisted row constants, linear ALiBi, packed f32x2 math
 #endif
+#ifndef ATTN_BWD_FUSED_DQ
+#define ATTN_BWD_FUSED_DQ 1  // head dim 128: dQ accumulated by the dK/dV kernel (no dq kernel)
+#endif
 #ifndef ATTN_BWD_DQ_KT
 #define ATTN_BWD_DQ_KT 128
 #endif
@@ -69,6 +79,7 @@ struct Args {
   const float* lse2;   // [B][Hq][Sq_pad], +inf for padded / fully masked rows
   const float* delta;  // [B][Hq][Sq_pad]
   void* dq; void* dk; void* dv;
+  float* dq_acc;       // fused dQ: [B][Hq][Sq_pad][D] fp32, zeroed before the kernel
   long long dq_s[3], dk_s[3], dv_s[3];
   attn_mask_t mask;
 };
@@ -93,10 +104,11 @@ __device__ __forceinline__ void band_q_range(const attn_mask_t& m, int k0, int k
   }
 }
 
-template <int D>
+template <int D, bool FQ>
 struct CfgKV {
+  static_assert(!FQ || D == 128, "fused dQ needs M = head dim = 128");
   static constexpr int KCH = D / 64;
-  static constexpr int ST = ATTN_BWD_KV_STAGES;
+  static constexpr int ST = FQ ? 2 : ATTN_BWD_KV_STAGES;
   static constexpr int PB = ATTN_BWD_P_BUFS;
   static constexpr int KV_BYTES = KCH * KROWS * 128;  // K or V tile
   static constexpr int QD_BYTES = KCH * QT * 128;     // Q or dO tile
@@ -107,27 +119,32 @@ struct CfgKV {
   static constexpr int OFF_P = OFF_ST + ST * STAGE;           // P^T  [PB][128 kv][64 q] bf16
   static constexpr int OFF_DS = OFF_P + PB * KROWS * 128;     // dS^T [PB][128 kv][64 q] bf16
   static constexpr int OFF_COLV = OFF_DS + PB * KROWS * 128;  // per elementwise warp: 32 column terms
-  static constexpr int OFF_BAR = OFF_COLV + 8 * 32 * 4;
-  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + PB + 1 + 1;
+  static constexpr int OFF_DQS = OFF_COLV + 8 * 32 * 4;        // fused dQ staging [QT q][D] fp32
+  static constexpr int DQS_BYTES = FQ ? QT * D * 4 : 0;
+  static constexpr int OFF_BAR = OFF_DQS + DQS_BYTES;
+  static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + PB + 1 + 1 + 6;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
-  // TMEM columns: S^T[2] at 0/64, dP^T[2] at 128/192, dV at 256, dK at 256 + D
   // TMEM columns.  With K/V in TMEM: K [0, D/2), V [D/2, D) as bf16 pairs, S^T at 128 and
   // dP^T at 192 (single buffers); otherwise S^T [2] at 0/64 and dP^T [2] at 128/192.
-  static constexpr bool KV_TMEM = ATTN_BWD_KV_TMEM != 0;
-  static constexpr int NSB = KV_TMEM ? 1 : 2;
+  // Fused dQ: S^T at 0, dP^T at 64 (single buffers), dQ^T [2] at 128/192.
+  static constexpr bool KV_TMEM = !FQ && ATTN_BWD_KV_TMEM != 0;
+  static constexpr int NSB = (KV_TMEM || FQ) ? 1 : 2;
   static constexpr uint32_t COL_K = 0, COL_V = D / 2;
-  static constexpr uint32_t COL_S = KV_TMEM ? 128 : 0, COL_DP = KV_TMEM ? 192 : 128;
+  static constexpr uint32_t COL_S = KV_TMEM ? 128 : 0;
+  static constexpr uint32_t COL_DP = KV_TMEM ? 192 : (FQ ? 64 : 128);
+  static constexpr uint32_t COL_DQ = 128;
   static constexpr uint32_t COL_DV = 256, COL_DK = 256 + D;
+  static_assert(SMEM <= 232448, "dkdv kernel shared memory");
 };
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool FQ>
 __global__ void __launch_bounds__(kThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const __grid_constant__ Args a) {
-  using C = CfgKV<D>;
+  using C = CfgKV<D, FQ>;
   constexpr int ST = C::ST;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -147,6 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto p_free = [&](int buf) { return bar0 + 8u * (6 + 2 * ST + buf); };
   const uint32_t acc_done = bar0 + 8u * (6 + 2 * ST + C::PB);
   const uint32_t kv_tmem = bar0 + 8u * (7 + 2 * ST + C::PB);  // K/V rows stored into TMEM
+  auto dq_full = [&](int x) { return bar0 + 8u * (8 + 2 * ST + C::PB + x); };   // dQ^T[x] computed
+  auto dq_free = [&](int x) { return bar0 + 8u * (10 + 2 * ST + C::PB + x); };  // dQ^T[x] read out
+  const uint32_t stage_full = bar0 + 8u * (12 + 2 * ST + C::PB);  // dQ staging written
+  const uint32_t stage_free = bar0 + 8u * (13 + 2 * ST + C::PB);  // previous reduction has read it
   constexpr int NSB = C::NSB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sp + C::OFF_TMEMPTR);
 
@@ -164,6 +185,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int q = 0; q < C::PB; ++q) mbar_init(p_free(q), 1);
     mbar_init(acc_done, 1);
     mbar_init(kv_tmem, 256);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(dq_full(x), 1);
+      mbar_init(dq_free(x), 256);
+    }
+    mbar_init(stage_full, 256);
+    mbar_init(stage_free, 1);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -220,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr int FMT = BF16 ? 1 : 0;
       constexpr uint32_t ID_S = idesc_f16(128, QT, FMT, 0, 0);
       constexpr uint32_t ID_G = idesc_f16(128, D, FMT, 0, 1);
+      constexpr uint32_t ID_DQ = idesc_f16(128, QT, FMT, 1, 1);  // dQ^T = K^T dS^T: both operands MN-major
       bool ok = mbar_wait(kv_full, 0, kStatusTimeoutMma);
       if (C::KV_TMEM) ok = ok && mbar_wait(kv_tmem, 0, kStatusTimeoutMma);
       auto issue_grads = [&](int j) -> bool {
@@ -235,6 +263,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t qb = sdesc_sw128(base + k * 16 * 128, QT * 128, 1024);
           umma_f16(tmem + C::COL_DV, pa, dob, ID_G, (j > 0 || k > 0) ? 1u : 0u);
           umma_f16(tmem + C::COL_DK, da, qb, ID_G, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        if (FQ) {
+          // dQ^T[j&1] (M = D rows of K^T, N = QT, K = KROWS kv rows); the buffer was
+          // last read out for tile j - 2.
+          if (!mbar_wait(dq_free(j & 1), ((j >> 1) & 1) ^ 1, kStatusTimeoutMma)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < KROWS / 16; ++k) {
+            const uint64_t ka = sdesc_sw128(sb + C::OFF_K + k * 16 * 128, KROWS * 128, 1024);
+            const uint64_t dsb = sdesc_sw128(sb + C::OFF_DS + (j % C::PB) * KROWS * 128 + k * 16 * 128,
+                                             KROWS * 128, 1024);
+            umma_f16(tmem + C::COL_DQ + (j & 1) * QT, ka, dsb, ID_DQ, k > 0 ? 1u : 0u);
+          }
+          umma_commit(dq_full(j & 1));
         }
         umma_commit(st_free(s));
         umma_commit(p_free(j % C::PB));
@@ -307,6 +349,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(kv_tmem);
     }
+    // Fused dQ: tile j's dQ^T (this thread: head-dim row r, q columns
+    // [32*half, 32*half + 32)) -> staging [q][D] fp32 -> one bulk add of the
+    // whole [QT][D] block into dq_acc by thread 0.
+    float* stg = reinterpret_cast<float*>(sp + C::OFF_DQS);
+    auto flush_dq = [&](int j, int hq_j, int q0_j) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(dq_full(j & 1), (j >> 1) & 1, kStatusTimeoutSoftmax))) return false;
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld32(tmem + lane_base + C::COL_DQ + (j & 1) * QT + half * 32, v);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(dq_free(j & 1));
+      if (threadIdx.x == 0) {
+        bulk_wait_read_all();  // the reduction of tile j - 1 has read the staging buffer
+        mbar_arrive(stage_free);
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(stage_free, j & 1, kStatusTimeoutSoftmax))) return false;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) stg[(half * 32 + c) * D + r] = __uint_as_float(v[c]);
+      fence_proxy_async_smem();
+      mbar_arrive(stage_full);
+      bool ok0 = true;
+      if (threadIdx.x == 0) {
+        ok0 = mbar_wait(stage_full, j & 1, kStatusTimeoutSoftmax);
+        if (ok0) {
+          bulk_reduce_add_f32(a.dq_acc + (((long long)b * a.Hq + hq_j) * a.Sq_pad + q0_j) * D, smem_u32(stg),
+                              QT * D * 4);
+          bulk_commit();
+        }
+      }
+      return __all_sync(0xffffffffu, ok0);  // warp-uniform
+    };
+    int prev_hq = 0, prev_q0 = 0;
     for (int it = 0; it < iters; ++it) {
       const int st = state_of(it);
       if (st == kSkip) continue;
@@ -389,8 +464,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
+      if (FQ && i > 0) {
+        ok = flush_dq(i - 1, prev_hq, prev_q0);
+        if (!ok) break;
+      }
+      prev_hq = hq;
+      prev_q0 = q0;
       ++i;
     }
+    if (FQ && ok && i > 0) ok = flush_dq(i - 1, prev_hq, prev_q0);
+    if (FQ && threadIdx.x == 0) bulk_wait_all();
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, kStatusTimeoutSoftmax));
     if (ok) {
       tc_fence_after();
@@ -709,6 +792,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// dQ = scale * dq_acc (fused path), one warp per row, 4 columns per lane.
+template <typename T>
+__global__ void dq_convert_kernel(const float* acc, T* dq, long long s0, long long s1, long long s2, int H,
+                                  int S, int S_pad, int D, float scale) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  if (row >= S) return;
+  const float* src = acc + (((long long)b * H + h) * S_pad + row) * D;
+  T* dst = dq + b * s0 + h * s1 + (long long)row * s2;
+  for (int e = lane * 4; e < D; e += 128) {
+    const float4 x = *reinterpret_cast<const float4*>(src + e);
+    uint2 w;
+    w.x = pack2(x.x * scale, x.y * scale, std::is_same<T, __nv_bfloat16>::value);
+    w.y = pack2(x.z * scale, x.w * scale, std::is_same<T, __nv_bfloat16>::value);
+    *reinterpret_cast<uint2*>(dst + e) = w;
   }
 }
 
