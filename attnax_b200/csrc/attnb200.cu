@@ -466,9 +466,14 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
       if (cudaMemsetAsync(dq_acc, 0, (size_t)B * Hq * Sq_pad * D * sizeof(float), st) != cudaSuccess)
         return ATTN_ERR_CUDA;
       kf<<<grid_kv, kThreads, CfgKV<D, true>::SMEM, st>>>(q64, k128, v128, do64, a);
-      dq_convert_kernel<T><<<dim3((Sq + 7) / 8, Hq, B), 256, 0, st>>>(
-          dq_acc, reinterpret_cast<T*>(p->dq), p->dq_strides[0], p->dq_strides[1], p->dq_strides[2], Hq, Sq,
-          Sq_pad, D, p->softmax_scale);
+      if (CfgKV<D, true>::RED)
+        dq_convert_t_kernel<T, D><<<dim3((Sq + 63) / 64, Hq, B), 256, 0, st>>>(
+            dq_acc, reinterpret_cast<T*>(p->dq), p->dq_strides[0], p->dq_strides[1], p->dq_strides[2], Hq, Sq,
+            Sq_pad, p->softmax_scale);
+      else
+        dq_convert_kernel<T><<<dim3((Sq + 7) / 8, Hq, B), 256, 0, st>>>(
+            dq_acc, reinterpret_cast<T*>(p->dq), p->dq_strides[0], p->dq_strides[1], p->dq_strides[2], Hq, Sq,
+            Sq_pad, D, p->softmax_scale);
       return launch_status(3);
     }
   }

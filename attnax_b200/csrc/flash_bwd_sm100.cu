@@ -14,7 +14,7 @@
 //         so dK/dV of a shared KV head are summed over its query heads, the
 //         transpose of the reference's jnp.repeat (attention.py:32-39).
 //         Fused dQ (D = 128): also dQ^T = K^T dS^T per tile (M = head dim,
-//         N = 64 q, two TMEM buffers); the elementwise warps stage it as
+//         N = 64 q; V sits in TMEM as the A operand of dP^T); the elementwise warps stage it as
 //         [64 q][D] fp32 in shared memory and one thread adds the 32 KB into
 //         an fp32 dQ accumulator with a bulk reduction (L2 performs the
 //         adds; summation order across kv tiles is not fixed).  K and V stay
@@ -57,6 +57,13 @@ constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
 #endif
 #ifndef ATTN_BWD_FAST_FULL
 #define ATTN_BWD_FAST_FULL 1  // full tiles: hoisted row constants, linear ALiBi, packed f32x2 math
+#endif
+#ifndef ATTN_BWD_FQ_V_TMEM
+#define ATTN_BWD_FQ_V_TMEM 1  // fused dQ: V in TMEM as the A operand of dP^T (dQ^T single-buffered)
+#endif
+#ifndef ATTN_BWD_DQ_RED
+#define ATTN_BWD_DQ_RED 0  // fused dQ: vector fp32 reductions from registers into a [D][q] accumulator
+                           // (measured slower than the staged bulk reduction: L2 atomics)
 #endif
 #ifndef ATTN_BWD_FUSED_DQ
 #define ATTN_BWD_FUSED_DQ 1  // head dim 128: dQ accumulated by the dK/dV kernel (no dq kernel)
@@ -108,7 +115,8 @@ template <int D, bool FQ>
 struct CfgKV {
   static_assert(!FQ || D == 128, "fused dQ needs M = head dim = 128");
   static constexpr int KCH = D / 64;
-  static constexpr int ST = FQ ? 2 : ATTN_BWD_KV_STAGES;
+  static constexpr bool RED = FQ && ATTN_BWD_DQ_RED != 0;  // no shared-memory staging of dQ^T
+  static constexpr int ST = (FQ && !RED) ? 2 : ATTN_BWD_KV_STAGES;
   static constexpr int PB = ATTN_BWD_P_BUFS;
   static constexpr int KV_BYTES = KCH * KROWS * 128;  // K or V tile
   static constexpr int QD_BYTES = KCH * QT * 128;     // Q or dO tile
@@ -120,7 +128,7 @@ struct CfgKV {
   static constexpr int OFF_DS = OFF_P + PB * KROWS * 128;     // dS^T [PB][128 kv][64 q] bf16
   static constexpr int OFF_COLV = OFF_DS + PB * KROWS * 128;  // per elementwise warp: 32 column terms
   static constexpr int OFF_DQS = OFF_COLV + 8 * 32 * 4;        // fused dQ staging [QT q][D] fp32
-  static constexpr int DQS_BYTES = FQ ? QT * D * 4 : 0;
+  static constexpr int DQS_BYTES = (FQ && !RED) ? QT * D * 4 : 0;
   static constexpr int OFF_BAR = OFF_DQS + DQS_BYTES;
   static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + PB + 1 + 1 + 6;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
@@ -128,13 +136,16 @@ struct CfgKV {
   static constexpr uint32_t TMEM_COLS = 512;
   // TMEM columns.  With K/V in TMEM: K [0, D/2), V [D/2, D) as bf16 pairs, S^T at 128 and
   // dP^T at 192 (single buffers); otherwise S^T [2] at 0/64 and dP^T [2] at 128/192.
-  // Fused dQ: S^T at 0, dP^T at 64 (single buffers), dQ^T [2] at 128/192.
+  // Fused dQ: S^T at 0, dP^T at 64 (single buffers), then either V at 128 and
+  // dQ^T at 192 (V_TMEM), or dQ^T [2] at 128/192.
   static constexpr bool KV_TMEM = !FQ && ATTN_BWD_KV_TMEM != 0;
+  static constexpr bool V_TMEM = KV_TMEM || (FQ && ATTN_BWD_FQ_V_TMEM != 0);
+  static constexpr int NDQ = (FQ && V_TMEM) ? 1 : 2;  // dQ^T TMEM buffers
   static constexpr int NSB = (KV_TMEM || FQ) ? 1 : 2;
-  static constexpr uint32_t COL_K = 0, COL_V = D / 2;
+  static constexpr uint32_t COL_K = 0, COL_V = KV_TMEM ? D / 2 : 128;
   static constexpr uint32_t COL_S = KV_TMEM ? 128 : 0;
   static constexpr uint32_t COL_DP = KV_TMEM ? 192 : (FQ ? 64 : 128);
-  static constexpr uint32_t COL_DQ = 128;
+  static constexpr uint32_t COL_DQ = V_TMEM ? 192 : 128;
   static constexpr uint32_t COL_DV = 256, COL_DK = 256 + D;
   static_assert(SMEM <= 232448, "dkdv kernel shared memory");
 };
@@ -249,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t ID_G = idesc_f16(128, D, FMT, 0, 1);
       constexpr uint32_t ID_DQ = idesc_f16(128, QT, FMT, 1, 1);  // dQ^T = K^T dS^T: both operands MN-major
       bool ok = mbar_wait(kv_full, 0, kStatusTimeoutMma);
-      if (C::KV_TMEM) ok = ok && mbar_wait(kv_tmem, 0, kStatusTimeoutMma);
+      if (C::V_TMEM) ok = ok && mbar_wait(kv_tmem, 0, kStatusTimeoutMma);
       auto issue_grads = [&](int j) -> bool {
         const int s = j % ST;
         const uint32_t base = sb + C::OFF_ST + s * C::STAGE;
@@ -267,16 +278,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (FQ) {
           // dQ^T[j&1] (M = D rows of K^T, N = QT, K = KROWS kv rows); the buffer was
           // last read out for tile j - 2.
-          if (!mbar_wait(dq_free(j & 1), ((j >> 1) & 1) ^ 1, kStatusTimeoutMma)) return false;
+          if (!mbar_wait(dq_free(j % C::NDQ), ((j / C::NDQ) & 1) ^ 1, kStatusTimeoutMma)) return false;
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < KROWS / 16; ++k) {
             const uint64_t ka = sdesc_sw128(sb + C::OFF_K + k * 16 * 128, KROWS * 128, 1024);
             const uint64_t dsb = sdesc_sw128(sb + C::OFF_DS + (j % C::PB) * KROWS * 128 + k * 16 * 128,
                                              KROWS * 128, 1024);
-            umma_f16(tmem + C::COL_DQ + (j & 1) * QT, ka, dsb, ID_DQ, k > 0 ? 1u : 0u);
+            umma_f16(tmem + C::COL_DQ + (j % C::NDQ) * QT, ka, dsb, ID_DQ, k > 0 ? 1u : 0u);
           }
-          umma_commit(dq_full(j & 1));
+          umma_commit(dq_full(j % C::NDQ));
         }
         umma_commit(st_free(s));
         umma_commit(p_free(j % C::PB));
@@ -298,6 +309,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t db = sdesc_sw128(base + C::QD_BYTES + (k >> 2) * QT * 128 + off, 16, 1024);
           if (C::KV_TMEM) {
             umma_f16_ts(tmem + C::COL_S, tmem + C::COL_K + k * 8, qb, ID_S, k > 0 ? 1u : 0u);
+            umma_f16_ts(tmem + C::COL_DP, tmem + C::COL_V + k * 8, db, ID_S, k > 0 ? 1u : 0u);
+          } else if (C::V_TMEM) {
+            const uint64_t ka = sdesc_sw128(sb + C::OFF_K + (k >> 2) * KROWS * 128 + off, 16, 1024);
+            umma_f16(tmem + C::COL_S, ka, qb, ID_S, k > 0 ? 1u : 0u);
             umma_f16_ts(tmem + C::COL_DP, tmem + C::COL_V + k * 8, db, ID_S, k > 0 ? 1u : 0u);
           } else {
             const uint64_t ka = sdesc_sw128(sb + C::OFF_K + (k >> 2) * KROWS * 128 + off, 16, 1024);
@@ -329,10 +344,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2);
     int i = 0;
     bool ok = true;
-    if (C::KV_TMEM) {
-      // Warps 0-3 store their K row, warps 4-7 their V row, into TMEM as bf16 pairs.
+    if (C::V_TMEM) {
+      // Warps 0-3 store their K row, warps 4-7 their V row, into TMEM as bf16
+      // pairs; with V alone in TMEM the two halves store 64-column chunks of V.
       ok = __all_sync(0xffffffffu, mbar_wait(kv_full, 0, kStatusTimeoutSoftmax));
-      if (ok) {
+      if (ok && !C::KV_TMEM) {
+        const uint8_t* src = sp + C::OFF_V + half * KROWS * 128;
+        uint32_t w[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src + r * 128 + ((u ^ (r & 7)) << 4));
+          w[u * 4 + 0] = v.x; w[u * 4 + 1] = v.y; w[u * 4 + 2] = v.z; w[u * 4 + 3] = v.w;
+        }
+        tmem_st32(tmem + lane_base + C::COL_V + half * 32, w);
+        tmem_wait_st();
+      } else if (ok) {
         const uint8_t* src = sp + (half ? C::OFF_V : C::OFF_K);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
@@ -354,13 +380,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     // whole [QT][D] block into dq_acc by thread 0.
     float* stg = reinterpret_cast<float*>(sp + C::OFF_DQS);
     auto flush_dq = [&](int j, int hq_j, int q0_j) -> bool {
-      if (!__all_sync(0xffffffffu, mbar_wait(dq_full(j & 1), (j >> 1) & 1, kStatusTimeoutSoftmax))) return false;
+      if (!__all_sync(0xffffffffu, mbar_wait(dq_full(j % C::NDQ), (j / C::NDQ) & 1, kStatusTimeoutSoftmax)))
+        return false;
       tc_fence_after();
       uint32_t v[32];
-      tmem_ld32(tmem + lane_base + C::COL_DQ + (j & 1) * QT + half * 32, v);
+      tmem_ld32(tmem + lane_base + C::COL_DQ + (j % C::NDQ) * QT + half * 32, v);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(dq_free(j & 1));
+      mbar_arrive(dq_free(j % C::NDQ));
+      if constexpr (C::RED) {
+        // dq_acc is [B][Hq][D][Sq_pad]: this thread's 32 q values are contiguous.
+        float* dst = a.dq_acc + (((long long)b * a.Hq + hq_j) * D + r) * a.Sq_pad + q0_j + half * 32;
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+          atomicAdd(reinterpret_cast<float4*>(dst + 4 * m),
+                    make_float4(__uint_as_float(v[4 * m]), __uint_as_float(v[4 * m + 1]),
+                                __uint_as_float(v[4 * m + 2]), __uint_as_float(v[4 * m + 3])));
+        return true;
+      }
       if (threadIdx.x == 0) {
         bulk_wait_read_all();  // the reduction of tile j - 1 has read the staging buffer
         mbar_arrive(stage_free);
@@ -792,6 +829,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// dQ = scale * dq_acc^T (fused path with a [B][H][D][S_pad] accumulator):
+// one 64-row q tile per block, transposed through shared memory.
+template <typename T, int D>
+__global__ void dq_convert_t_kernel(const float* acc, T* dq, long long s0, long long s1, long long s2, int H,
+                                    int S, int S_pad, float scale) {
+  __shared__ float tile[D][65];
+  const int q0 = blockIdx.x * 64, h = blockIdx.y, b = blockIdx.z;
+  const float* src = acc + ((long long)b * H + h) * D * S_pad + q0;
+  for (int i = threadIdx.x; i < D * 64; i += blockDim.x) {
+    const int d = i / 64, q = i % 64;
+    tile[d][q] = src[(long long)d * S_pad + q];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 64 * (D / 2); i += blockDim.x) {
+    const int q = i / (D / 2), d = 2 * (i % (D / 2));
+    if (q0 + q < S)
+      *reinterpret_cast<uint32_t*>(dq + b * s0 + h * s1 + (long long)(q0 + q) * s2 + d) =
+          pack2(tile[d][q] * scale, tile[d + 1][q] * scale, std::is_same<T, __nv_bfloat16>::value);
   }
 }
 
