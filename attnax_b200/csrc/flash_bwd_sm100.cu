@@ -217,11 +217,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   band_q_range(a.mask, k0, k1, a.Sq, &t_lo, &t_hi);
   const int ntiles = t_hi - t_lo;
   const int iters = a.group * ntiles;  // (g, q tile) pairs, g outer
-  auto state_of = [&](int it) {
-    const int qt = t_lo + it % max(ntiles, 1);
+  auto state_of = [&](int qt) {
     const int q0 = qt * QT;
     return tile_state(a.mask, nullptr, nullptr, 0, 0, b, q0, min(q0 + QT, a.Sq), k0, k1, KROWS);
   };
+  // Inside [t_lo, t_hi) only a prefix mask (or a document mask) can drop a
+  // whole tile; the TMA and MMA warps classify tiles only then.
+  const bool may_skip = a.mask.prefix_len != nullptr || a.mask.doc_q != nullptr;
+  // (g, qt) advance of the flat (g, q tile) loop.
+#define DKDV_NEXT(g, qt) ((qt) + 1 == t_hi ? ((qt) = t_lo, ++(g)) : ++(qt))
 
   if (warp == 8) {
     if (lane == 0) {
@@ -235,9 +239,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(sb + C::OFF_V + c * KROWS * 128, &tm_v, kv_full, c * 64, k0, hkv, b);
       }
       int i = 0;
-      for (int it = 0; it < iters; ++it) {
-        if (state_of(it) == kSkip) continue;
-        const int g = it / ntiles, qt = t_lo + it % ntiles;
+      for (int it = 0, g = 0, qt = t_lo; it < iters; ++it, DKDV_NEXT(g, qt)) {
+        if (may_skip && state_of(qt) == kSkip) continue;
         const int hq = hkv * a.group + g, q0 = qt * QT;
         const int s = i % ST;
         if (!mbar_wait(st_free(s), ((i / ST) & 1) ^ 1, kStatusTimeoutLoad)) break;
@@ -261,32 +264,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t ID_DQ = idesc_f16(128, QT, FMT, 1, 1);  // dQ^T = K^T dS^T: both operands MN-major
       bool ok = mbar_wait(kv_full, 0, kStatusTimeoutMma);
       if (C::V_TMEM) ok = ok && mbar_wait(kv_tmem, 0, kStatusTimeoutMma);
+      // Descriptor bases; every operand below is a base plus a constant offset.
+      const uint64_t dK_k = sdesc_sw128(sb + C::OFF_K, 16, 1024);             // K, K-major
+      const uint64_t dV_k = sdesc_sw128(sb + C::OFF_V, 16, 1024);             // V, K-major
+      const uint64_t dK_mn = sdesc_sw128(sb + C::OFF_K, KROWS * 128, 1024);   // K^T, MN-major
+      const uint64_t dST_k = sdesc_sw128(sb + C::OFF_ST, 16, 1024);           // Q / dO stages, K-major
+      const uint64_t dST_mn = sdesc_sw128(sb + C::OFF_ST, QT * 128, 1024);    // Q / dO stages, MN-major
+      const uint64_t dP_k = sdesc_sw128(sb + C::OFF_P, 16, 1024);             // P^T, K-major
+      const uint64_t dDS_k = sdesc_sw128(sb + C::OFF_DS, 16, 1024);           // dS^T, K-major
+      const uint64_t dDS_mn = sdesc_sw128(sb + C::OFF_DS, KROWS * 128, 1024); // dS^T, MN-major
       auto issue_grads = [&](int j) -> bool {
         const int s = j % ST;
-        const uint32_t base = sb + C::OFF_ST + s * C::STAGE;
+        const uint32_t so = s * C::STAGE, po = (j % C::PB) * KROWS * 128;
         if (!mbar_wait(p_full, j & 1, kStatusTimeoutMma)) return false;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < QT / 16; ++k) {
-          const uint64_t pa = sdesc_sw128(sb + C::OFF_P + (j % C::PB) * KROWS * 128 + k * 32, 16, 1024);
-          const uint64_t da = sdesc_sw128(sb + C::OFF_DS + (j % C::PB) * KROWS * 128 + k * 32, 16, 1024);
-          const uint64_t dob = sdesc_sw128(base + C::QD_BYTES + k * 16 * 128, QT * 128, 1024);
-          const uint64_t qb = sdesc_sw128(base + k * 16 * 128, QT * 128, 1024);
-          umma_f16(tmem + C::COL_DV, pa, dob, ID_G, (j > 0 || k > 0) ? 1u : 0u);
-          umma_f16(tmem + C::COL_DK, da, qb, ID_G, (j > 0 || k > 0) ? 1u : 0u);
+          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          umma_f16(tmem + C::COL_DV, sdesc_add(dP_k, po + k * 32), sdesc_add(dST_mn, so + C::QD_BYTES + k * 2048),
+                   ID_G, acc);
+          umma_f16(tmem + C::COL_DK, sdesc_add(dDS_k, po + k * 32), sdesc_add(dST_mn, so + k * 2048), ID_G, acc);
         }
         if (FQ) {
-          // dQ^T[j&1] (M = D rows of K^T, N = QT, K = KROWS kv rows); the buffer was
-          // last read out for tile j - 2.
+          // dQ^T (M = D rows of K^T, N = QT, K = KROWS kv rows); its TMEM buffer
+          // was last read out for tile j - NDQ.
           if (!mbar_wait(dq_free(j % C::NDQ), ((j / C::NDQ) & 1) ^ 1, kStatusTimeoutMma)) return false;
           tc_fence_after();
 #pragma unroll
-          for (int k = 0; k < KROWS / 16; ++k) {
-            const uint64_t ka = sdesc_sw128(sb + C::OFF_K + k * 16 * 128, KROWS * 128, 1024);
-            const uint64_t dsb = sdesc_sw128(sb + C::OFF_DS + (j % C::PB) * KROWS * 128 + k * 16 * 128,
-                                             KROWS * 128, 1024);
-            umma_f16(tmem + C::COL_DQ + (j % C::NDQ) * QT, ka, dsb, ID_DQ, k > 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < KROWS / 16; ++k)
+            umma_f16(tmem + C::COL_DQ + (j % C::NDQ) * QT, sdesc_add(dK_mn, k * 2048),
+                     sdesc_add(dDS_mn, po + k * 2048), ID_DQ, k > 0 ? 1u : 0u);
           umma_commit(dq_full(j % C::NDQ));
         }
         umma_commit(st_free(s));
@@ -294,31 +301,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       int i = 0;
-      for (int it = 0; ok && it < iters; ++it) {
-        if (state_of(it) == kSkip) continue;
+      for (int it = 0, g = 0, qt = t_lo; ok && it < iters; ++it, DKDV_NEXT(g, qt)) {
+        if (may_skip && state_of(qt) == kSkip) continue;
         const int s = i % ST;
         ok = mbar_wait(st_full(s), (i / ST) & 1, kStatusTimeoutMma) &&
              mbar_wait(s_free(i % NSB), ((i / NSB) & 1) ^ 1, kStatusTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t base = sb + C::OFF_ST + s * C::STAGE;
+        const uint32_t so = s * C::STAGE;
+        const uint32_t cs = C::COL_S + (i % NSB) * QT, cdp = C::COL_DP + (i % NSB) * QT;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k & 3) * 32;
-          const uint64_t qb = sdesc_sw128(base + (k >> 2) * QT * 128 + off, 16, 1024);
-          const uint64_t db = sdesc_sw128(base + C::QD_BYTES + (k >> 2) * QT * 128 + off, 16, 1024);
+          const uint32_t off = (k >> 2) * QT * 128 + (k & 3) * 32;   // within a Q / dO tile
+          const uint32_t koff = (k >> 2) * KROWS * 128 + (k & 3) * 32;  // within the K / V tile
+          const uint64_t qb = sdesc_add(dST_k, so + off), db = sdesc_add(dST_k, so + C::QD_BYTES + off);
+          const uint32_t acc = k > 0 ? 1u : 0u;
           if (C::KV_TMEM) {
-            umma_f16_ts(tmem + C::COL_S, tmem + C::COL_K + k * 8, qb, ID_S, k > 0 ? 1u : 0u);
-            umma_f16_ts(tmem + C::COL_DP, tmem + C::COL_V + k * 8, db, ID_S, k > 0 ? 1u : 0u);
+            umma_f16_ts(tmem + cs, tmem + C::COL_K + k * 8, qb, ID_S, acc);
+            umma_f16_ts(tmem + cdp, tmem + C::COL_V + k * 8, db, ID_S, acc);
           } else if (C::V_TMEM) {
-            const uint64_t ka = sdesc_sw128(sb + C::OFF_K + (k >> 2) * KROWS * 128 + off, 16, 1024);
-            umma_f16(tmem + C::COL_S, ka, qb, ID_S, k > 0 ? 1u : 0u);
-            umma_f16_ts(tmem + C::COL_DP, tmem + C::COL_V + k * 8, db, ID_S, k > 0 ? 1u : 0u);
+            umma_f16(tmem + cs, sdesc_add(dK_k, koff), qb, ID_S, acc);
+            umma_f16_ts(tmem + cdp, tmem + C::COL_V + k * 8, db, ID_S, acc);
           } else {
-            const uint64_t ka = sdesc_sw128(sb + C::OFF_K + (k >> 2) * KROWS * 128 + off, 16, 1024);
-            const uint64_t va = sdesc_sw128(sb + C::OFF_V + (k >> 2) * KROWS * 128 + off, 16, 1024);
-            umma_f16(tmem + C::COL_S + (i % NSB) * QT, ka, qb, ID_S, k > 0 ? 1u : 0u);
-            umma_f16(tmem + C::COL_DP + (i % NSB) * QT, va, db, ID_S, k > 0 ? 1u : 0u);
+            umma_f16(tmem + cs, sdesc_add(dK_k, koff), qb, ID_S, acc);
+            umma_f16(tmem + cdp, sdesc_add(dV_k, koff), db, ID_S, acc);
           }
         }
         umma_commit(s_full(i % NSB));
@@ -419,10 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       return __all_sync(0xffffffffu, ok0);  // warp-uniform
     };
     int prev_hq = 0, prev_q0 = 0;
-    for (int it = 0; it < iters; ++it) {
-      const int st = state_of(it);
+    for (int it = 0, g = 0, qt = t_lo; it < iters; ++it, DKDV_NEXT(g, qt)) {
+      const int st = state_of(qt);
       if (st == kSkip) continue;
-      const int g = it / ntiles, qt = t_lo + it % ntiles;
       const int hq = hkv * a.group + g, q0 = qt * QT;
       const int s = i % ST;
       ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full(i % NSB), (i / NSB) & 1, kStatusTimeoutSoftmax));
@@ -556,6 +561,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
+
+#undef DKDV_NEXT
 
 // ------------------------------------------------------------------- dQ ----
 template <int D>

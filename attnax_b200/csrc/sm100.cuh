@@ -204,6 +204,11 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// Descriptor `d` advanced by `bytes` (a multiple of 16).  The start-address
+// field holds shared-memory addresses >> 4, below 2^14 for the 228 KB a CTA
+// can own, so the addition never carries into the neighbouring fields.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+
 // Instruction descriptor for kind::f16 with f32 accumulation.
 // a/b format: 0 = f16, 1 = bf16.  a_mn / b_mn: operand is MN-major.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_format, int a_mn, int b_mn) {
