@@ -35,7 +35,7 @@ constexpr int kThreads = 384;      // 3 warpgroups: softmax A, softmax B, TMA + 
 // Register split (setmaxnreg): launched at kLaunchRegs per thread; the TMA/MMA
 // warpgroup gives registers up, the softmax warpgroups take them:
 // 128 * kProducerRegs + 256 * kSoftmaxRegs == 384 * kLaunchRegs.
-constexpr int kLaunchRegs = 168, kProducerRegs = 88, kSoftmaxRegs = 208;
+constexpr int kLaunchRegs = 168, kProducerRegs = 104, kSoftmaxRegs = 200;
 static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs == kThreads * kLaunchRegs, "register split");
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 #ifndef ATTN_FWD2_REG_PARTIAL
@@ -157,10 +157,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   // kv tile visited at position t of the loop (all three roles use the same order).
   auto kv_tile = [&](int t) { return ATTN_FWD2_REVERSE ? j_hi - 1 - t : j_lo + t; };
   const int n_tiles = j_hi - j_lo;
-  auto state_of = [&](int x, int j) {
-    if (!act[x] || j < jl[x] || j >= jh[x]) return (int)kSkip;
-    return tile_state(a.mask, a.doc_q_tiles, a.doc_kv_tiles, a.nq_doc, a.nk_doc, b, q0[x], q1[x], j * BN,
+  // State of kv tile j for the query tile (active, kv range [lo, hi), rows [r0, r1)).
+  auto state_at = [&](bool x_act, int lo, int hi, int r0, int r1, int j) {
+    if (!x_act || j < lo || j >= hi) return (int)kSkip;
+    return tile_state(a.mask, a.doc_q_tiles, a.doc_kv_tiles, a.nq_doc, a.nk_doc, b, r0, r1, j * BN,
                       min((j + 1) * BN, a.Skv), BN);
+  };
+  // x is a compile-time constant at every call (the arrays stay in registers).
+  auto state_of = [&](int x, int j) { return state_at(act[x], jl[x], jh[x], q0[x], q1[x], j); };
+  // Inside a tile's band range only a prefix or document mask can drop a kv
+  // tile; otherwise the TMA and MMA warps need only the range test.
+  const bool may_skip = a.mask.prefix_len != nullptr || a.mask.doc_q != nullptr;
+  auto kept = [&](int x, int j) {
+    return may_skip ? state_of(x, j) != kSkip : (act[x] && j >= jl[x] && j < jh[x]);
   };
 
   if (warp >= 8) {
@@ -178,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int n = 0;
       for (int t = 0; t < n_tiles; ++t) {
         const int j = kv_tile(t);
-        if (state_of(0, j) == kSkip && state_of(1, j) == kSkip) continue;
+        if (!kept(0, j) && !kept(1, j)) continue;
         const int s = n % S;
         if (!mbar_wait(kv_empty(s), ((n / S) & 1) ^ 1, kStatusTimeoutLoad)) break;
         mbar_expect_tx(k_full(s), C::KV_BYTES);
@@ -201,14 +210,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pv[2] = {0, 0};      // PV products issued per tile
       int prev_s = -1, n = 0;  // stage of the previous kv tile, kv tiles consumed
       bool prev_act[2] = {false, false};
+      // Descriptor bases; each operand is a base plus a constant offset.
+      const uint64_t dQ = sdesc_sw128(sb + C::OFF_Q, 16, 1024);
+      const uint64_t dK = sdesc_sw128(sb + C::OFF_K, 16, 1024);
+      const uint64_t dV = sdesc_sw128(sb + C::OFF_V, BN * 128, 1024);  // MN-major
       auto issue_s = [&](int x, int s) {
         const uint32_t d = tmem + C::s_col(x);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint64_t ad =
-              sdesc_sw128(sb + C::OFF_Q + x * C::Q_BYTES + (k >> 2) * BM * 128 + (k & 3) * 32, 16, 1024);
-          const uint64_t bd =
-              sdesc_sw128(sb + C::OFF_K + s * C::KV_BYTES + (k >> 2) * BN * 128 + (k & 3) * 32, 16, 1024);
+          const uint64_t ad = sdesc_add(dQ, x * C::Q_BYTES + (k >> 2) * BM * 128 + (k & 3) * 32);
+          const uint64_t bd = sdesc_add(dK, s * C::KV_BYTES + (k >> 2) * BN * 128 + (k & 3) * 32);
           umma_f16(d, ad, bd, IDESC_QK, k > 0 ? 1u : 0u);
         }
         umma_commit(s_full(x));
@@ -220,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t pa = tmem + C::s_col(x);  // P: bf16 pairs in the first 64 columns of S
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k) {
-          const uint64_t bd = sdesc_sw128(sb + C::OFF_V + s * C::KV_BYTES + k * 16 * 128, BN * 128, 1024);
+          const uint64_t bd = sdesc_add(dV, s * C::KV_BYTES + k * 16 * 128);
           asm volatile(
               "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
               " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem + C::o_col(x)),
@@ -233,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       for (int t = 0; ok && t < n_tiles; ++t) {
         const int j = kv_tile(t);
-        const bool ax = state_of(0, j) != kSkip, bx = state_of(1, j) != kSkip;
+        const bool ax = kept(0, j), bx = kept(1, j);
         if (!ax && !bx) continue;
         const int s = n % S;
         ok = mbar_wait(k_full(s), (n / S) & 1, kStatusTimeoutMma);
@@ -267,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = threadIdx.x & 127; // row within the tile == TMEM lane
     const int my_q0 = x ? q0[1] : q0[0];
     const bool my_act = x ? act[1] : act[0];
+    const int my_q1 = x ? q1[1] : q1[0], my_jl = x ? jl[1] : jl[0], my_jh = x ? jh[1] : jh[0];
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     float m_run = -FLT_MAX, l_run = 0.f;
     int i = 0;
@@ -287,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const long long pref = a.mask.prefix_len ? (long long)a.mask.prefix_len[b] : -1;
     for (int t = 0; t < n_tiles; ++t) {
       const int j = kv_tile(t);
-      const int st = state_of(x, j);
+      const int st = state_at(my_act, my_jl, my_jh, my_q0, my_q1, j);
       if (st == kSkip) continue;
       ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), i & 1, kStatusTimeoutSoftmax));
       if (!ok) break;
