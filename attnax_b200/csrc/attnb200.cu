@@ -431,10 +431,14 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
   using namespace bwd;
   const int Sq_pad = bwd_seq_pad(p);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  prep_pad_kernel<T><<<dim3(Sq_pad / 4, p->num_heads_q, p->batch), 128, 0, st>>>(
-      reinterpret_cast<const T*>(p->out), reinterpret_cast<const T*>(p->d_out), p->o_strides[0],
-      p->o_strides[1], p->o_strides[2], p->do_strides[0], p->do_strides[1], p->do_strides[2], p->lse,
-      delta, lse2, p->num_heads_q, p->seq_q, Sq_pad, D);
+  {
+    constexpr int rows_per_block = kPrepRowsPerBlock / (D / 8);
+    prep_rows_kernel<T, D><<<dim3((Sq_pad + rows_per_block - 1) / rows_per_block, p->num_heads_q, p->batch), 256, 0,
+                             st>>>(
+        reinterpret_cast<const T*>(p->out), reinterpret_cast<const T*>(p->d_out), p->o_strides[0], p->o_strides[1],
+        p->o_strides[2], p->do_strides[0], p->do_strides[1], p->do_strides[2], p->lse, delta, lse2,
+        p->num_heads_q, p->seq_q, Sq_pad, (D == 128 && bwd_fused_dq(p) && !CfgKV<128, true>::RED) ? dq_acc : nullptr);
+  }
   Args a;
   a.B = p->batch; a.Hq = p->num_heads_q; a.Hkv = p->num_heads_kv; a.Sq = p->seq_q; a.Skv = p->seq_kv;
   a.Sq_pad = Sq_pad; a.group = p->num_heads_q / p->num_heads_kv;
@@ -463,7 +467,9 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
       static int attr_dev_f = -1;
       auto kf = dkdv_kernel<D, BF16, true>;
       if (!smem_attr_once(kf, CfgKV<D, true>::SMEM, &attr_dev_f)) return ATTN_ERR_CUDA;
-      if (cudaMemsetAsync(dq_acc, 0, (size_t)B * Hq * Sq_pad * D * sizeof(float), st) != cudaSuccess)
+      // (dq_acc rows were zeroed by prep_rows_kernel; the transposed layout is cleared here)
+      if (CfgKV<D, true>::RED &&
+          cudaMemsetAsync(dq_acc, 0, (size_t)B * Hq * Sq_pad * D * sizeof(float), st) != cudaSuccess)
         return ATTN_ERR_CUDA;
       kf<<<grid_kv, kThreads, CfgKV<D, true>::SMEM, st>>>(q64, k128, v128, do64, a);
       if (CfgKV<D, true>::RED)

@@ -880,41 +880,62 @@ __global__ void dq_convert_kernel(const float* acc, T* dq, long long s0, long lo
 }
 
 // delta = rowsum(dO * O), lse2 = lse * log2(e) into [B][H][S_pad] with
-// padded rows (+inf, 0) so bulk copies of whole 64-row tiles stay in bounds.
-template <typename T>
-__global__ void prep_pad_kernel(const T* out, const T* dout, long long os0, long long os1, long long os2,
-                                long long ds0, long long ds1, long long ds2, const float* lse,
-                                float* delta, float* lse2, int H, int S, int S_pad, int D) {
-  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
+// padded rows (+inf, 0), and zeroes the row of the fused-dQ accumulator when
+// there is one.  D/8 lanes share a row (16 bytes each) and every warp keeps
+// kPasses rows-per-pass of loads in flight before reducing.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) prep_rows_kernel(const T* out, const T* dout, long long os0, long long os1,
+                                                        long long os2, long long ds0, long long ds1, long long ds2,
+                                                        const float* lse, float* delta, float* lse2, int H, int S,
+                                                        int S_pad, float* dq_acc) {
+  constexpr int L = D / 8;          // lanes per row
+  constexpr int RPP = 32 / L;       // rows per warp pass
+  constexpr int kPasses = 4;
+  constexpr int RPW = RPP * kPasses;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
-  if (row >= S_pad) return;
-  const long long idx = ((long long)b * H + h) * S_pad + row;
-  if (row >= S) {
-    if (lane == 0) {
-      delta[idx] = 0.f;
-      lse2[idx] = INFINITY;
+  const int row0 = (blockIdx.x * (blockDim.x >> 5) + warp) * RPW + lane / L;
+  const int cl = (lane % L) * 8;
+  uint4 ov[kPasses], dv[kPasses];
+#pragma unroll
+  for (int p = 0; p < kPasses; ++p) {
+    const int row = row0 + p * RPP;
+    if (row < S) {
+      ov[p] = *reinterpret_cast<const uint4*>(out + b * os0 + h * os1 + (long long)row * os2 + cl);
+      dv[p] = *reinterpret_cast<const uint4*>(dout + b * ds0 + h * ds1 + (long long)row * ds2 + cl);
+    } else {
+      ov[p] = dv[p] = make_uint4(0, 0, 0, 0);
     }
-    return;
   }
-  const T* o = out + b * os0 + h * os1 + (long long)row * os2;
-  const T* d = dout + b * ds0 + h * ds1 + (long long)row * ds2;
-  float acc = 0.f;
-  for (int e = lane * 8; e < D; e += 256) {
-    const uint4 ov = *reinterpret_cast<const uint4*>(o + e);
-    const uint4 dv = *reinterpret_cast<const uint4*>(d + e);
-    const T* oh = reinterpret_cast<const T*>(&ov);
-    const T* dh = reinterpret_cast<const T*>(&dv);
+#pragma unroll
+  for (int p = 0; p < kPasses; ++p) {
+    const T* oh = reinterpret_cast<const T*>(&ov[p]);
+    const T* dh = reinterpret_cast<const T*>(&dv[p]);
+    float acc = 0.f;
 #pragma unroll
     for (int x = 0; x < 8; ++x) acc = fmaf(to_f32(oh[x]), to_f32(dh[x]), acc);
-  }
-  for (int x = 16; x > 0; x >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, x);
-  if (lane == 0) {
-    delta[idx] = acc;
-    const float l = lse[((long long)b * H + h) * S + row];
-    lse2[idx] = (l == -INFINITY) ? INFINITY : l * kLog2e;
+#pragma unroll
+    for (int o = L / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    const int row = row0 + p * RPP;
+    if (dq_acc && row < S_pad) {  // zero this row of the fused-dQ accumulator ([row][D] fp32)
+      float4* z = reinterpret_cast<float4*>(dq_acc + (((long long)b * H + h) * S_pad + row) * D + cl);
+      z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (lane % L == 0 && row < S_pad) {
+      const long long idx = ((long long)b * H + h) * S_pad + row;
+      if (row < S) {
+        delta[idx] = acc;
+        const float l = lse[((long long)b * H + h) * S + row];
+        lse2[idx] = (l == -INFINITY) ? INFINITY : l * kLog2e;
+      } else {
+        delta[idx] = 0.f;
+        lse2[idx] = INFINITY;
+      }
+    }
   }
 }
+constexpr int kPrepRowsPerBlock = 8 * 4 * 32;  // 8 warps x 4 passes x 32 lanes, divided by D/8 lanes per row
 
 }  // namespace bwd
 }  // namespace attnb200

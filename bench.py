@@ -109,9 +109,16 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # Start timing only once the sampler is producing rows.
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < 3.0:
+            self.f.flush()
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *a):
@@ -238,20 +245,12 @@ def run_flash(args, torch, dist, rank, world, peaks):
     launches = launches * args.steps // (args.steps + args.warmup)
     value = world * (fwd_flops + bwd_flops) / (ms * 1e-3) / 1e12
 
-    # e2e: public API, inputs copied from pinned host memory, scalar read back
-    qg = {}
-
-    def e2e_step(marks):
-        tq = hq.to(dev, non_blocking=True).requires_grad_()
-        tk = hk.to(dev, non_blocking=True).requires_grad_()
-        tv = hv.to(dev, non_blocking=True).requires_grad_()
-        tdo = hdo.to(dev, non_blocking=True)
-        out = ax.flash_attention(tq, tk, tv, score_mod=mod)
-        out.backward(tdo)
-        qg["loss"] = (out.detach().float() * tdo.float()).sum().to("cpu", non_blocking=False)
-
-    e2e_steps = max(2, min(args.steps, 5))
-    e2e_ms, _ = tm.run(e2e_step, e2e_steps, 2)
+    # e2e: public API (autograd flash_attention), every step's inputs copied
+    # from pinned host memory and its scalar result read back to the host.
+    # Copies run on a side stream one step ahead of the compute stream
+    # (double-buffered device inputs), so PCIe overlaps the kernels.
+    e2e_steps = max(2, min(args.steps, 8))
+    e2e_ms = e2e_pipelined(torch, dist, world, dev, (hq, hk, hv, hdo), mod, ax, e2e_steps, warmup=2)
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
     e2e_value = world * (fwd_flops + bwd_flops) / (e2e_ms * 1e-3) / 1e12
 
@@ -262,8 +261,9 @@ def run_flash(args, torch, dist, rank, world, peaks):
         kern[name] = {"ms": round(ph[name], 4), "tflops": round(a, 2), "frac": round(a / peak_b, 4),
                       "frac_sustained": round(a / peak_s, 4)}
     dom = max(kern, key=lambda n: kern[n]["ms"])
-    kernel_names = {"fwd": "fwd::flash_fwd_kernel<128,bf16> (tcgen05)",
-                    "bwd": "attn_bwd: bwd::prep_pad_kernel + bwd::dkdv_kernel + bwd::dq_kernel (tcgen05)"}
+    kernel_names = {"fwd": "fwd2::flash_fwd2_kernel<128,bf16> (tcgen05)",
+                    "bwd": "attn_bwd: bwd::prep_rows_kernel + bwd::dkdv_kernel<128,bf16,fused dQ> "
+                           "+ bwd::dq_convert_kernel (tcgen05)"}
     roof = {"kernel": kernel_names[dom], "bound": "tensor", "achieved": kern[dom]["tflops"],
             "peak": peak_b, "unit": "TFLOP/s", "frac": kern[dom]["frac"],
             "peak_sustained": peak_s, "frac_sustained": kern[dom]["frac_sustained"],
@@ -290,7 +290,60 @@ def run_flash(args, torch, dist, rank, world, peaks):
     return line
 
 
-TRAFFIC = {}  # per-launch DRAM bytes from ncu captures, keyed by phase; filled from profiles/
+# Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of each
+# phase at the B4 bench size: ncu capture of the B1 case of the same workload
+# (profiles/flash_fwd_bwd_kernels_small.md) x 4 batches.  fwd: flash_fwd2_kernel
+# 133.7 MB; bwd: prep_pad 139.5 MB + fused dkdv 427.9 MB + dq_convert 174.6 MB.
+TRAFFIC = {"fwd": 4 * 133.7e6, "bwd": 4 * (139.5e6 + 427.9e6 + 174.6e6)}
+
+
+def e2e_pipelined(torch, dist, world, dev, host, mod, ax, steps, warmup):
+    """ms per step of the public-API fwd+bwd with H2D copies one step ahead."""
+    copy = torch.cuda.Stream()
+    comp = torch.cuda.current_stream()
+    bufs = [[torch.empty_like(h, device=dev) for h in host] for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    for e in free:
+        e.record(comp)
+
+    def upload(slot):
+        with torch.cuda.stream(copy):
+            copy.wait_event(free[slot])
+            for d, h in zip(bufs[slot], host):
+                d.copy_(h, non_blocking=True)
+            copied[slot].record(copy)
+
+    def run(n):
+        upload(0)
+        for i in range(n):
+            slot = i % 2
+            if i + 1 < n:
+                upload((i + 1) % 2)
+            comp.wait_event(copied[slot])
+            tq, tk, tv, tdo = bufs[slot]
+            tq, tk, tv = (t.detach().requires_grad_() for t in (tq, tk, tv))
+            out = ax.flash_attention(tq, tk, tv, score_mod=mod)
+            out.backward(tdo)
+            loss = (out.detach().float() * tdo.float()).sum()
+            free[slot].record(comp)
+            loss.to("cpu", non_blocking=False)
+
+    run(warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(comp)
+    run(steps)
+    end.record(comp)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms / steps
 
 
 def run_paged(args, torch, peaks):
