@@ -190,17 +190,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < NSB; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 256);
+      mbar_init(s_free(i), 8);  // one arrival per elementwise warp
     }
-    mbar_init(p_full, 256);
+    mbar_init(p_full, 8);
     for (int q = 0; q < C::PB; ++q) mbar_init(p_free(q), 1);
     mbar_init(acc_done, 1);
-    mbar_init(kv_tmem, 256);
+    mbar_init(kv_tmem, 8);
     for (int x = 0; x < 2; ++x) {
       mbar_init(dq_full(x), 1);
-      mbar_init(dq_free(x), 256);
+      mbar_init(dq_free(x), 8);
     }
-    mbar_init(stage_full, 256);
+    mbar_init(stage_full, 8);
     mbar_init(stage_free, 1);
     fence_mbar_init();
   }
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
       }
       tc_fence_before();
-      mbar_arrive(kv_tmem);
+      mbar_arrive_warp(kv_tmem);
     }
     // Fused dQ: tile j's dQ^T (this thread: head-dim row r, q columns
     // [32*half, 32*half + 32)) -> staging [q][D] fp32 -> one bulk add of the
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tmem + lane_base + C::COL_DQ + (j % C::NDQ) * QT + half * 32, v);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(dq_free(j % C::NDQ));
+      mbar_arrive_warp(dq_free(j % C::NDQ));
       if constexpr (C::RED) {
         // dq_acc is [B][Hq][D][Sq_pad]: this thread's 32 q values are contiguous.
         float* dst = a.dq_acc + (((long long)b * a.Hq + hq_j) * D + r) * a.Sq_pad + q0_j + half * 32;
@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 32; ++c) stg[(half * 32 + c) * D + r] = __uint_as_float(v[c]);
       fence_proxy_async_smem();
-      mbar_arrive(stage_full);
+      mbar_arrive_warp(stage_full);
       bool ok0 = true;
       if (threadIdx.x == 0) {
         ok0 = mbar_wait(stage_full, j & 1, kStatusTimeoutSoftmax);
@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tmem + lane_base + C::COL_DP + (i % NSB) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(dp));
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(s_free(i % NSB));
+      mbar_arrive_warp(s_free(i % NSB));
       const int c0 = q0 + half * HC;
       const float* sl = reinterpret_cast<const float*>(sp + C::OFF_ST + s * C::STAGE + 2 * C::QD_BYTES) + half * HC;
       const float* sd = sl + QT;
@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive_warp(p_full);
       if (FQ && i > 0) {
         ok = flush_dq(i - 1, prev_hq, prev_q0);
         if (!ok) break;
@@ -625,9 +625,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < NSB; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 256);
+      mbar_init(s_free(i), 8);  // one arrival per elementwise warp
     }
-    mbar_init(ds_full, 256);
+    mbar_init(ds_full, 8);
     for (int q = 0; q < C::DB; ++q) mbar_init(ds_free(q), 1);
     mbar_init(acc_done, 1);
     fence_mbar_init();
@@ -760,7 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         if (cc == HC / 32 - 1) {
           tc_fence_before();
-          mbar_arrive(s_free(i % NSB));
+          mbar_arrive_warp(s_free(i % NSB));
         }
         const int c0 = j * KT + half * HC + cc * 32;
         if (st == kFull && fast_mask) {
@@ -798,7 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive_warp(ds_full);
       ++i;
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, kStatusTimeoutSoftmax));

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(s_full(x), 1);
-      mbar_init(p_full(x), 128);
+      mbar_init(p_full(x), 4);  // one arrival per softmax warp
       mbar_init(o_done(x), 1);
     }
     fence_mbar_init();
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full(x));
+      mbar_arrive_warp(p_full(x));
       ++i;
     }
     // ------------------------------------------------------------ epilogue --

@@ -94,9 +94,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 128);
+      mbar_init(s_free(i), 4);  // one arrival per softmax warp
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 4);
     mbar_init(pv_done, 1);
     fence_mbar_init();
   }
@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(s_free(i & 1));
+      mbar_arrive_warp(s_free(i & 1));
 
       const int k0 = j * BN;
       const RowCtx rc = make_row_ctx(a.mask, a.sl2, b, hq, q0 + r, k0, min(BN, a.Skv - k0), false);
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive_warp(p_full);
       ++i;
     }
     // ------------------------------------------------------------ epilogue --
