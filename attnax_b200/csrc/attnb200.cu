@@ -690,9 +690,9 @@ static PagedWs paged_ws_layout(const attn_paged_params_t* p) {
 }
 
 // 3-D map over a pool [blocks*block_size tokens, heads_kv, head_dim]:
-// box = 64 features x 1 head x block_size tokens, 128B swizzle.
+// box = 64 features x 1 head x box_tokens tokens, 128B swizzle.
 static bool make_pool_tmap(CUtensorMap* m, attn_dtype_t dt, const void* pool, long long tokens,
-                           int heads_kv, int head_dim, int block_size) {
+                           int heads_kv, int head_dim, int box_tokens) {
   auto enc = encode_fn();
   if (!enc) return false;
   const uint64_t es = dtype_size(dt);
@@ -701,7 +701,7 @@ static bool make_pool_tmap(CUtensorMap* m, attn_dtype_t dt, const void* pool, lo
   if (heads_kv == 1) strides[0] = strides[1];
   for (int i = 0; i < 2; ++i)
     if (strides[i] % 16 != 0) return false;
-  cuuint32_t box[3] = {64, 1, (cuuint32_t)block_size};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_tokens};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType t =
       dt == ATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -710,12 +710,14 @@ static bool make_pool_tmap(CUtensorMap* m, attn_dtype_t dt, const void* pool, lo
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int R, bool BF16>
+// MMA: tensor-core consumers (block_size % 16 == 0), R = 16 rows per CTA.
+template <int R, bool BF16, bool MMA = false>
 static int launch_paged(const attn_paged_params_t* p, const PagedWs& w, char* ws, cudaStream_t st) {
   CUtensorMap tk, tv;
   const long long tokens = (long long)p->num_blocks * p->block_size;
-  if (!make_pool_tmap(&tk, p->dtype, p->key_pool, tokens, p->num_heads_kv, 128, p->block_size) ||
-      !make_pool_tmap(&tv, p->dtype, p->value_pool, tokens, p->num_heads_kv, 128, p->block_size))
+  const int box_tokens = MMA ? paged::mma_unit(p->block_size) : p->block_size;
+  if (!make_pool_tmap(&tk, p->dtype, p->key_pool, tokens, p->num_heads_kv, 128, box_tokens) ||
+      !make_pool_tmap(&tv, p->dtype, p->value_pool, tokens, p->num_heads_kv, 128, box_tokens))
     return ATTN_ERR_INVALID;
   paged::DecArgs a;
   a.num_seqs = p->num_seqs; a.Hq = p->num_heads_q; a.Hkv = p->num_heads_kv; a.Sq = p->seq_q;
@@ -725,19 +727,21 @@ static int launch_paged(const attn_paged_params_t* p, const PagedWs& w, char* ws
   a.row_groups = (a.rows + R - 1) / R;
   a.max_splits = w.max_splits;
   a.chunk_tokens = paged::kChunkTokens;
-  a.box_bytes = (int)(((size_t)p->block_size * 128 + 1023) & ~(size_t)1023);
+  a.box_bytes = (int)(((size_t)box_tokens * 128 + 1023) & ~(size_t)1023);
   a.q = p->q; a.block_table = p->block_table; a.seq_lens = p->seq_lengths;
   a.part_o = reinterpret_cast<float*>(ws + w.part_o);
   a.part_lse = reinterpret_cast<float*>(ws + w.part_lse);
   a.sl2 = p->softmax_scale * kLog2e;
-  constexpr int S = paged::DecCfg<R>::STAGES;
+  const int S = MMA ? 128 / box_tokens : paged::DecCfg<R>::STAGES;
+  // (the MMA kernel merges its warps through the drained page ring instead of extra scratch)
   const size_t smem = 1024 + (size_t)2 * S * 2 * a.box_bytes + 2 * S * 8 +
-                      sizeof(float) * (paged::NW * (19 * R) + paged::NW * R * 128 + paged::NW * R * 2);
+                      (MMA ? 0 : sizeof(float) * (paged::NW * (19 * R) + paged::NW * R * 128 + paged::NW * R * 2));
   if (smem > 227 * 1024) return ATTN_ERR_UNSUPPORTED;
-  auto kern = paged::paged_decode_kernel<R, BF16>;
+  auto kern = (MMA && box_tokens == 32) ? paged::decode_kernel<R, BF16, MMA, 32>()
+                                          : paged::decode_kernel<R, BF16, MMA, 16>();
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return ATTN_ERR_CUDA;
-  dim3 grid(w.max_splits, p->num_heads_kv * a.row_groups, p->num_seqs);
+  dim3 grid(p->num_heads_kv * a.row_groups, w.max_splits, p->num_seqs);
   kern<<<grid, paged::kThreads, smem, st>>>(tk, tv, a);
   int rc = launch_status();
   if (rc != ATTN_OK) return rc;
@@ -772,6 +776,8 @@ int attn_paged_decode(const attn_paged_params_t* p, void* stream) {
   char* ws = reinterpret_cast<char*>(p->workspace);
   const int rows = (p->num_heads_q / p->num_heads_kv) * p->seq_q;
   const bool bf = p->dtype == ATTN_BF16;
+  if (p->block_size % 16 == 0)
+    return bf ? launch_paged<16, true, true>(p, w, ws, st) : launch_paged<16, false, true>(p, w, ws, st);
   if (rows <= 1) return bf ? launch_paged<1, true>(p, w, ws, st) : launch_paged<1, false>(p, w, ws, st);
   if (rows <= 2) return bf ? launch_paged<2, true>(p, w, ws, st) : launch_paged<2, false>(p, w, ws, st);
   if (rows <= 4) return bf ? launch_paged<4, true>(p, w, ws, st) : launch_paged<4, false>(p, w, ws, st);

@@ -99,8 +99,11 @@ __global__ void __launch_bounds__(kThreads)
   constexpr int D = 128;
   constexpr int S = DecCfg<R>::STAGES;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  const int split = blockIdx.x;
-  const int hkv = blockIdx.y / a.row_groups, rg = blockIdx.y % a.row_groups;
+  // Grid (kv head x row group, split, sequence): the CTAs of every kv head of
+  // one split are adjacent in launch order, so they stream the same pages
+  // (whose token rows hold all kv heads side by side) at the same time.
+  const int split = blockIdx.y;
+  const int hkv = blockIdx.x / a.row_groups, rg = blockIdx.x % a.row_groups;
   const int seq = blockIdx.z;
   const int ctx = a.seq_lens[seq];
   const int t0 = split * a.chunk_tokens;
@@ -265,6 +268,8 @@ __global__ void __launch_bounds__(kThreads)
       const int box = lane >> 4, unit = (lane & 15) >> 1, subv = (lane & 1) * 8;
       for (int rr = 0; rr < nt; ++rr) {
         const int row = g16 + rr;
+        // (P is 0 there, but a never-written slot may hold NaN: 0 * NaN)
+        if (page_tok0 + row < t0 || page_tok0 + row >= t1) continue;
         const uint2 w = *reinterpret_cast<const uint2*>(vst + box * a.box_bytes + row * 128 +
                                                          ((unit ^ (row & 7)) << 4) + subv);
         const T* h4 = reinterpret_cast<const T*>(&w);
@@ -324,6 +329,267 @@ __global__ void __launch_bounds__(kThreads)
       a.part_lse[prow * a.max_splits + split] = (lt > 0.f && mx > -FLT_MAX) ? mx + lg2(lt) : -INFINITY;
   }
 }
+
+// ------------------------------------------------- tensor-core consumers ----
+// mma.sync m16n8k16 with fp32 accumulation; A row-major (16 x 16), B
+// column-major (16 x 8).  The decode is HBM-bound: the tensor core only
+// replaces ~1300 scalar FMA/convert instructions per 16-token page slice.
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (BF16)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// Paged decode with tensor-core consumers (block_size a multiple of 16).
+// The TMA ring streams units of U tokens (16 or 32, dividing block_size) of
+// one kv head's slice, 128/U stages (64 KB) so every block size up to 256
+// keeps 3 CTAs per SM; split-K and outputs as paged_decode_kernel; up to 16
+// query rows (GQA group x decode positions of one kv head) per CTA, padded
+// to the m16 tile with zero rows.  Per 16 tokens a consumer warp runs
+// S = Q K^T (ldmatrix on the swizzled K slice, 16 MMAs), the online softmax
+// on the accumulator fragments (rows g and g+8 of lane = 4g + t), and
+// O += P V with P re-packed in registers as the A operand (ldmatrix.trans on
+// V, 16 MMAs).
+template <bool BF16, int U>
+__global__ void __launch_bounds__(kThreads, 3)
+    paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                            const __grid_constant__ DecArgs a) {
+  constexpr int D = 128, RT = 16;
+  constexpr int S = 128 / U;  // a.box_bytes == U * 128
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  const int split = blockIdx.y;
+  const int hkv = blockIdx.x / a.row_groups, rg = blockIdx.x % a.row_groups;
+  const int seq = blockIdx.z;
+  const int ctx = a.seq_lens[seq];
+  const int t0 = split * a.chunk_tokens;
+  if (t0 >= ctx && !(split == 0 && ctx == 0)) return;
+  const int t1 = min(ctx, t0 + a.chunk_tokens);
+  const int u0 = t0 / U, u1 = (t1 + U - 1) / U;
+  const int nunits = max(0, u1 - u0);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t sb = (raw_base + 1023u) & ~1023u;
+  uint8_t* sp = smem_raw + (sb - raw_base);
+  const int page_bytes = 2 * a.box_bytes;  // K or V slice of one unit
+  const uint32_t k_base = sb, v_base = sb + S * page_bytes;
+  const uint32_t bar0 = sb + 2 * S * page_bytes;
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (S + s); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == NW) {
+    if (lane == 0 && nunits > 0) {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      const int32_t* row = a.block_table + (long long)seq * a.max_blocks;
+      for (int i = 0; i < nunits; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, kStatusTimeoutLoad)) break;
+        const int tok = (u0 + i) * U;
+        const int pid = (int)phys_page(row, tok / a.BS, a.num_blocks);
+        const int prow = pid * a.BS + tok % a.BS;  // pool row of the unit's first token
+        mbar_expect_tx(full(s), 4 * U * 128);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(k_base + s * page_bytes + c * a.box_bytes, &tm_k, full(s), c * 64, hkv, prow);
+          tma_load_3d(v_base + s * page_bytes + c * a.box_bytes, &tm_v, full(s), c * 64, hkv, prow);
+        }
+      }
+    }
+    return;
+  }
+
+  const int g = lane >> 2, tig = lane & 3;
+  // Q as A fragments: [k-step][row g lo, row g+8 lo, row g hi, row g+8 hi].
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = rg * RT + g + 8 * h;
+    const bool okr = row < a.rows;
+    const int gq = okr ? row % a.group : 0, s_pos = okr ? row / a.group : 0;
+    const T* qr = reinterpret_cast<const T*>(a.q) + (((long long)seq * a.Hq + hkv * a.group + gq) * a.Sq + s_pos) * D;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      qf[kk][h] = okr ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 2 * tig) : 0u;
+      qf[kk][2 + h] = okr ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 8 + 2 * tig) : 0u;
+    }
+  }
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m[2] = {-FLT_MAX, -FLT_MAX}, l[2] = {0.f, 0.f};
+  // ldmatrix row of this lane: matrix lane >> 3, row lane & 7.
+  const int mi = lane >> 3, ri = lane & 7;
+  auto sw = [&](uint32_t base, int tok, int d) {  // swizzled [tok][d] in a 2-box page slice
+    return base + (d >> 6) * a.box_bytes + tok * 128 + ((((d & 63) >> 3) ^ (tok & 7)) << 4);
+  };
+  bool ok = true;
+  for (int i = warp; i < nunits; i += NW) {
+    const int s = i % S;
+    ok = __all_sync(0xffffffffu, mbar_wait(full(s), (i / S) & 1, kStatusTimeoutSoftmax));
+    if (!ok) break;
+    const uint32_t kst = k_base + s * page_bytes, vst = v_base + s * page_bytes;
+    const int unit_tok0 = (u0 + i) * U;
+    bool zeroed = false;
+#pragma unroll
+    for (int g16 = 0; g16 < U; g16 += 16) {
+      const int tok_a = unit_tok0 + g16;
+      if (tok_a < t0 || tok_a + 16 > t1) {
+        // V rows of tokens outside [t0, t1) -> 0, so P = 0 there meets finite V.
+        for (int x = lane; x < 16 * 16; x += 32) {
+          const int r = x >> 4, u = x & 15, tk = tok_a + r;
+          if (tk < t0 || tk >= t1)
+            *reinterpret_cast<uint4*>(sp + (sw(vst, g16 + r, u * 8) - sb)) = make_uint4(0, 0, 0, 0);
+        }
+        zeroed = true;
+        __syncwarp();
+      }
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        uint32_t b[4];  // (tokens 0-7, d lo), (0-7, hi), (8-15, lo), (8-15, hi)
+        ldsm_x4(b, sw(kst, g16 + 8 * (mi >> 1) + ri, 16 * kk + 8 * (mi & 1)));
+        mma16816<BF16>(sc[0], qf[kk], b[0], b[1]);
+        mma16816<BF16>(sc[1], qf[kk], b[2], b[3]);
+      }
+      // column (n, e) holds token g16 + 8n + 2*tig + (e & 1); e < 2: row g, else row g + 8
+      float mx[2] = {-INFINITY, -INFINITY};
+      bool valid[2][2];
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tk = tok_a + 8 * n + 2 * tig + e;
+          valid[n][e] = tk >= t0 && tk < t1;
+          if (valid[n][e]) {
+            mx[0] = fmaxf(mx[0], sc[n][e]);
+            mx[1] = fmaxf(mx[1], sc[n][2 + e]);
+          }
+        }
+      float alpha[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+        const float m_new = fmaxf(m[h], mx[h] * a.sl2);
+        alpha[h] = ex2(m[h] - m_new);
+        m[h] = m_new;
+      }
+      float pr[2][4];
+      float ps[2] = {0.f, 0.f};
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = e >> 1;
+          pr[n][e] = valid[n][e & 1] ? ex2(fmaf(sc[n][e], a.sl2, -m[h])) : 0.f;
+          ps[h] += pr[n][e];
+        }
+      l[0] = l[0] * alpha[0] + ps[0];
+      l[1] = l[1] * alpha[1] + ps[1];
+      if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) {
+          o[n][0] *= alpha[0]; o[n][1] *= alpha[0];
+          o[n][2] *= alpha[1]; o[n][3] *= alpha[1];
+        }
+      }
+      const uint32_t pa[4] = {pack2(pr[0][0], pr[0][1], BF16), pack2(pr[0][2], pr[0][3], BF16),
+                              pack2(pr[1][0], pr[1][1], BF16), pack2(pr[1][2], pr[1][3], BF16)};
+#pragma unroll
+      for (int np = 0; np < D / 16; ++np) {
+        uint32_t b[4];  // (tokens 0-7, d tile 2np), (8-15, 2np), (0-7, 2np+1), (8-15, 2np+1)
+        ldsm_x4_t(b, sw(vst, g16 + 8 * (mi & 1) + ri, 16 * np + 8 * (mi >> 1)));
+        mma16816<BF16>(o[2 * np], pa, b[0], b[1]);
+        mma16816<BF16>(o[2 * np + 1], pa, b[2], b[3]);
+      }
+    }
+    if (zeroed) fence_proxy_async_smem();  // generic writes before the next TMA into this stage
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty(s));
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+  }
+  // ---- merge the NW warps' partial states through the drained page ring ----
+  named_bar_sync(1, NW * 32);
+  constexpr int MS = D + 4;  // padded row stride
+  float* mo = reinterpret_cast<float*>(sp);  // [NW][RT][MS]
+  float* ml = mo + NW * RT * MS;             // [NW][RT][2]
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) {
+    *reinterpret_cast<float2*>(mo + (warp * RT + g) * MS + 8 * n + 2 * tig) = make_float2(o[n][0], o[n][1]);
+    *reinterpret_cast<float2*>(mo + (warp * RT + g + 8) * MS + 8 * n + 2 * tig) = make_float2(o[n][2], o[n][3]);
+  }
+  if (tig == 0) {
+    ml[(warp * RT + g) * 2] = m[0];
+    ml[(warp * RT + g) * 2 + 1] = l[0];
+    ml[(warp * RT + g + 8) * 2] = m[1];
+    ml[(warp * RT + g + 8) * 2 + 1] = l[1];
+  }
+  named_bar_sync(1, NW * 32);
+  if (!__all_sync(0xffffffffu, ok)) return;
+  for (int j = warp; j < RT; j += NW) {
+    const int row = rg * RT + j;
+    if (row >= a.rows) continue;
+    float mxr = -FLT_MAX;
+    for (int w = 0; w < NW; ++w) mxr = fmaxf(mxr, ml[(w * RT + j) * 2]);
+    float lt = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w = 0; w < NW; ++w) {
+      const float f = ex2(ml[(w * RT + j) * 2] - mxr);
+      lt += f * ml[(w * RT + j) * 2 + 1];
+      for (int e = 0; e < 4; ++e) acc[e] += f * mo[(w * RT + j) * MS + lane * 4 + e];
+    }
+    const int gq = row % a.group, s_pos = row / a.group;
+    const int hq = hkv * a.group + gq;
+    const long long prow = ((long long)seq * a.Hq * a.Sq + (long long)hq * a.Sq + s_pos);
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    float* po = a.part_o + (prow * a.max_splits + split) * D;
+    for (int e = 0; e < 4; ++e) po[lane * 4 + e] = acc[e] * inv;
+    if (lane == 0)
+      a.part_lse[prow * a.max_splits + split] = (lt > 0.f && mxr > -FLT_MAX) ? mxr + lg2(lt) : -INFINITY;
+  }
+}
+
+// The decode kernel for a launch: tensor-core consumers (R = 16) or scalar ones.
+template <int R, bool BF16, bool MMA, int U>
+constexpr auto decode_kernel() {
+  if constexpr (MMA) return &paged_decode_mma_kernel<BF16, U>;
+  else return &paged_decode_kernel<R, BF16>;
+}
+// Tokens per TMA unit of the tensor-core kernel for a block size (a multiple of 16).
+inline int mma_unit(int block_size) { return block_size % 32 == 0 ? 32 : 16; }
 
 // Merges split partials (log2-domain lse): o = sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M).
 template <typename T>

@@ -39,12 +39,13 @@ static int scratch_address(float** out) {
   return ATTN_OK;
 }
 
-template <int R, bool BF16>
+template <int R, bool BF16, bool MMA = false>
 static int launch(const attn_paged_params_t* p, float* scratch, int splits, int chunk, cudaStream_t st) {
   CUtensorMap tk, tv;
   const long long tokens = (long long)p->num_blocks * p->block_size;
-  if (!make_pool_tmap(&tk, p->dtype, p->key_pool, tokens, p->num_heads_kv, 128, p->block_size) ||
-      !make_pool_tmap(&tv, p->dtype, p->value_pool, tokens, p->num_heads_kv, 128, p->block_size))
+  const int box_tokens = MMA ? paged::mma_unit(p->block_size) : p->block_size;
+  if (!make_pool_tmap(&tk, p->dtype, p->key_pool, tokens, p->num_heads_kv, 128, box_tokens) ||
+      !make_pool_tmap(&tv, p->dtype, p->value_pool, tokens, p->num_heads_kv, 128, box_tokens))
     return ATTN_ERR_INVALID;
   const size_t rows = (size_t)p->num_seqs * p->num_heads_q * p->seq_q;
   paged::DecArgs a;
@@ -55,19 +56,20 @@ static int launch(const attn_paged_params_t* p, float* scratch, int splits, int 
   a.row_groups = (a.rows + R - 1) / R;
   a.max_splits = splits;
   a.chunk_tokens = chunk;
-  a.box_bytes = (int)(((size_t)p->block_size * 128 + 1023) & ~(size_t)1023);
+  a.box_bytes = (int)(((size_t)box_tokens * 128 + 1023) & ~(size_t)1023);
   a.q = p->q; a.block_table = p->block_table; a.seq_lens = p->seq_lengths;
   a.part_o = scratch;                                  // [rows][splits][128]
   a.part_lse = scratch + rows * (size_t)splits * 128;  // [rows][splits]
   a.sl2 = p->softmax_scale * kLog2e;
-  constexpr int S = paged::DecCfg<R>::STAGES;
+  const int S = MMA ? 128 / box_tokens : paged::DecCfg<R>::STAGES;
   const size_t smem = 1024 + (size_t)2 * S * 2 * a.box_bytes + 2 * S * 8 +
-                      sizeof(float) * (paged::NW * (19 * R) + paged::NW * R * 128 + paged::NW * R * 2);
+                      (MMA ? 0 : sizeof(float) * (paged::NW * (19 * R) + paged::NW * R * 128 + paged::NW * R * 2));
   if (smem > 227 * 1024) return ATTN_ERR_UNSUPPORTED;
-  auto kern = paged::paged_decode_kernel<R, BF16>;
+  auto kern = (MMA && box_tokens == 32) ? paged::decode_kernel<R, BF16, MMA, 32>()
+                                          : paged::decode_kernel<R, BF16, MMA, 16>();
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return ATTN_ERR_CUDA;
-  kern<<<dim3(splits, p->num_heads_kv * a.row_groups, p->num_seqs), paged::kThreads, smem, st>>>(tk, tv, a);
+  kern<<<dim3(p->num_heads_kv * a.row_groups, splits, p->num_seqs), paged::kThreads, smem, st>>>(tk, tv, a);
   int rc = launch_status();
   if (rc != ATTN_OK) return rc;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -115,6 +117,9 @@ extern "C" int attn_paged_decode_static(const attn_paged_params_t* p, void* stre
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int grp_rows = (p->num_heads_q / p->num_heads_kv) * p->seq_q;
   const bool bf = p->dtype == ATTN_BF16;
+  if (p->block_size % 16 == 0)
+    return bf ? paged_static::launch<16, true, true>(p, scratch, splits, chunk, st)
+              : paged_static::launch<16, false, true>(p, scratch, splits, chunk, st);
   if (grp_rows <= 1)
     return bf ? paged_static::launch<1, true>(p, scratch, splits, chunk, st)
               : paged_static::launch<1, false>(p, scratch, splits, chunk, st);

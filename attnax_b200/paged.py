@@ -168,8 +168,12 @@ def paged_decode_raw(query, cache: PagedKVCache, *, block_table=None, seq_length
 
 
 def _fast_decode_ok(query, cache: PagedKVCache) -> bool:
+    # Block sizes: multiples of 16 up to 256 (tensor-core decode, 16/32-token
+    # TMA units), other sizes up to 48 (whole-page TMA ring); the rest gather.
+    bs = cache.block_size
     return (cache.head_dim == 128 and cache.key_pool.dtype in (torch.bfloat16, torch.float16)
-            and cache.block_size <= 256 and query.dtype in (torch.bfloat16, torch.float16, torch.float32))
+            and ((bs % 16 == 0 and bs <= 256) or bs <= 48)
+            and query.dtype in (torch.bfloat16, torch.float16, torch.float32))
 
 
 def paged_attention(query, cache: PagedKVCache, sequence_idx: int, *, mask=None, score_mod=None,

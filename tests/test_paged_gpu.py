@@ -82,6 +82,34 @@ def test_decode_matches_oracle(hq, hkv, sq):
     assert_bf16_close(got, want, f"decode hq={hq} hkv={hkv} sq={sq}")
 
 
+@pytest.mark.parametrize("bs,hq,hkv,sq,dtype", [
+    (8, 32, 8, 1, torch.bfloat16),     # scalar consumers (block_size not a multiple of 16)
+    (32, 32, 8, 1, torch.bfloat16),    # tensor-core consumers, two 16-token groups per page
+    (64, 64, 2, 1, torch.bfloat16),    # 32 rows per kv head: two row groups; 32-token TMA units
+    (48, 32, 8, 1, torch.bfloat16),    # three 16-token TMA units per page
+    (16, 24, 2, 2, torch.float16),     # 24 rows (12 heads x 2 positions), fp16
+])
+def test_decode_block_sizes_rows_dtypes_nan_slots(bs, hq, hkv, sq, dtype):
+    """Unused slots of each sequence's last page hold NaN (a pool that was
+    never written there); only tokens < seq_len may reach the output."""
+    rng = np.random.default_rng(bs + hq + sq)
+    lens = [1, bs - 3, bs + 5, 3 * bs + 1, 2048 + 7, 4099]
+    cache, oc = _random_cache(rng, lens, hkv, bs=bs, dtype=dtype)
+    kp, vp = cache.key_pool.clone(), cache.value_pool.clone()
+    table = oc.block_table
+    for s_, n in enumerate(lens):
+        if n % bs:
+            last = table[s_, (n - 1) // bs]
+            kp[last, n % bs:] = float("nan")
+            vp[last, n % bs:] = float("nan")
+    cache = ax.PagedKVCache(kp, vp, cache.block_table, cache.seq_lengths)
+    q = randn(rng, (len(lens), hq, sq, 128), True)
+    got = npy(ax.paged_attention_batched(torch.tensor(q, dtype=dtype, device=DEV), cache))
+    assert np.isfinite(got).all()
+    want = O.paged_attention_batched(q, oc)
+    assert_bf16_close(got, want, f"decode bs={bs} hq={hq} hkv={hkv} sq={sq} {dtype}")
+
+
 def test_decode_single_sequence_api():
     rng = np.random.default_rng(9)
     cache, oc = _random_cache(rng, [700, 33], 8)
