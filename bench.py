@@ -292,9 +292,12 @@ def run_flash(args, torch, dist, rank, world, peaks):
 
 # Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of each
 # phase at the B4 bench size: ncu capture of the B1 case of the same workload
-# (profiles/flash_fwd_bwd_kernels_small.md) x 4 batches.  fwd: flash_fwd2_kernel
-# 133.7 MB; bwd: prep_pad 139.5 MB + fused dkdv 427.9 MB + dq_convert 174.6 MB.
-TRAFFIC = {"fwd": 4 * 133.7e6, "bwd": 4 * (139.5e6 + 427.9e6 + 174.6e6)}
+# (profiles/flash_bwd_kernels_small.md) x 4 batches.  fwd: flash_fwd2_kernel
+# 133.2 MB; bwd: prep_rows 222.7 MB + fused dkdv 427.7 MB + dq_convert 176.3 MB.
+TRAFFIC = {"fwd": 4 * 133.2e6, "bwd": 4 * (222.7e6 + 427.7e6 + 176.3e6)}
+# Paged decode: DRAM bytes / algorithmic bytes of the 16-sequence capture
+# (profiles/paged_decode_kernel_small.md); traffic scales with the tokens read.
+PAGED_TRAFFIC_RATIO = (1.100622e9 + 6.36672e6) / 1.1001e9
 
 
 def e2e_pipelined(torch, dist, world, dev, host, mod, ax, steps, warmup):
@@ -378,7 +381,8 @@ def run_paged(args, torch, peaks):
             "ms_per_step": round(ms, 4), "algorithmic_bytes": alg_bytes, "tokens": tokens,
             "config": f"{c['nseq']} seqs, ctx U[512,32768], page {c['bs']}, Hq{c['Hq']} Hkv{c['Hkv']} D{c['D']} bf16",
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None},
+                         "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "traffic": round(PAGED_TRAFFIC_RATIO * alg_bytes)},
             "gpu_launches": int(launches)}
 
 
