@@ -54,8 +54,10 @@ __host__ __device__ inline int tile_state(const attn_mask_t& m, const int2* doc_
     if (!(khi < pref || khi <= qlo)) st = kPartial;
   }
   if (m.doc_q) {
-    if (doc_q_tiles && doc_kv_tiles && (q0 % kDocTile) == 0 && (k0 % kDocTile) == 0 &&
-        q1 - q0 <= kDocTile && k1 - k0 <= kDocTile) {
+    // a tile inside one kDocTile tile uses that tile's (min, max) ids (a
+    // superset of its own: skip only if disjoint, full only if one document)
+    if (doc_q_tiles && doc_kv_tiles && q0 / kDocTile == (q1 - 1) / kDocTile &&
+        k0 / kDocTile == (k1 - 1) / kDocTile) {
       const int2 a = doc_q_tiles[(long long)b * nq_doc + q0 / kDocTile];
       const int2 c = doc_kv_tiles[(long long)b * nk_doc + k0 / kDocTile];
       if (a.y < c.x || c.y < a.x) return kSkip;
@@ -141,6 +143,31 @@ template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// For every row tile t (of batch b): the range [lo, hi) of column tiles
+// whose (min, max) id range overlaps row tile t's, from the per-tile ranges
+// of doc_tile_range_kernel -- exact for sorted ids (packed documents), a
+// superset otherwise.  One warp per row tile.
+__global__ void doc_cross_range_kernel(const int2* row_tiles, int n_row, const int2* col_tiles, int n_col,
+                                       int2* out) {
+  const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  if (t >= n_row) return;
+  const int2 r = row_tiles[(long long)b * n_row + t];
+  int lo = 0x7fffffff, hi = -1;
+  for (int c = lane; c < n_col; c += 32) {
+    const int2 k = col_tiles[(long long)b * n_col + c];
+    if (!(r.y < k.x || k.y < r.x)) {
+      lo = min(lo, c);
+      hi = max(hi, c);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  if (lane == 0) out[(long long)b * n_row + t] = hi < 0 ? make_int2(0, 0) : make_int2(lo, hi + 1);
+}
 
 // (min, max) of document ids over kDocTile-row tiles of global positions
 // offset + [t*kDocTile, min((t+1)*kDocTile, len)).

@@ -146,8 +146,29 @@ static int launch_status(int n = 1) {
   return ATTN_OK;
 }
 
+// Document-mask tile tables: (min, max) ids per kDocTile tile of q and kv,
+// then for each q tile the overlapping kv tile range (q_jr) and, if asked,
+// for each kv tile the overlapping q tile range (kv_qr).
+static int launch_doc_ranges(const attn_mask_t& m, int batch, int seq_q, int seq_kv, int2* dq_t, int2* dkv_t,
+                             int2* q_jr, int2* kv_qr, cudaStream_t st) {
+  const int nq = (seq_q + kDocTile - 1) / kDocTile, nk = (seq_kv + kDocTile - 1) / kDocTile;
+  doc_tile_range_kernel<<<dim3(nq, batch), 128, 0, st>>>(m.doc_q, m.doc_q_bstride, m.q_offset, seq_q, nq, dq_t);
+  doc_tile_range_kernel<<<dim3(nk, batch), 128, 0, st>>>(m.doc_kv, m.doc_kv_bstride, m.kv_offset, seq_kv, nk,
+                                                         dkv_t);
+  int n = 2;
+  if (q_jr) {
+    doc_cross_range_kernel<<<dim3((nq + 7) / 8, batch), 256, 0, st>>>(dq_t, nq, dkv_t, nk, q_jr);
+    ++n;
+  }
+  if (kv_qr) {
+    doc_cross_range_kernel<<<dim3((nk + 7) / 8, batch), 256, 0, st>>>(dkv_t, nk, dq_t, nq, kv_qr);
+    ++n;
+  }
+  return launch_status(n);
+}
+
 struct FwdWorkspace {
-  size_t doc_q = 0, doc_kv = 0, lse = 0, total = 0;
+  size_t doc_q = 0, doc_kv = 0, doc_jr = 0, lse = 0, total = 0;
 };
 
 static FwdWorkspace fwd_workspace_layout(const attn_fwd_params_t* p) {
@@ -159,6 +180,8 @@ static FwdWorkspace fwd_workspace_layout(const attn_fwd_params_t* p) {
     off += align256((size_t)p->batch * nq * sizeof(int2));
     w.doc_kv = off;
     off += align256((size_t)p->batch * nk * sizeof(int2));
+    w.doc_jr = off;
+    off += align256((size_t)p->batch * nq * sizeof(int2));
   }
   if (p->fix_masked_rows && !p->lse) {
     w.lse = off;
@@ -195,7 +218,7 @@ static int launch_simt_fwd(const attn_fwd_params_t* p, float* lse, cudaStream_t 
 
 template <int D, bool BF16>
 static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2* dq_t, const int2* dkv_t,
-                             cudaStream_t st) {
+                             const int2* djr, cudaStream_t st) {
   CUtensorMap tq, tk, tv;
   if (!make_tmap(&tq, p->dtype, p->q, p->batch, p->num_heads_q, p->seq_q, D, p->q_strides, fwd2::BM) ||
       !make_tmap(&tk, p->dtype, p->k, p->batch, p->num_heads_kv, p->seq_kv, D, p->k_strides, fwd2::BN) ||
@@ -209,7 +232,7 @@ static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2*
   a.out = p->out;
   a.o_s0 = p->o_strides[0]; a.o_s1 = p->o_strides[1]; a.o_s2 = p->o_strides[2];
   a.lse = lse; a.mask = p->mask;
-  a.doc_q_tiles = dq_t; a.doc_kv_tiles = dkv_t;
+  a.doc_q_tiles = dq_t; a.doc_kv_tiles = dkv_t; a.doc_jrange = djr;
   a.nq_doc = (p->seq_q + kDocTile - 1) / kDocTile;
   a.nk_doc = (p->seq_kv + kDocTile - 1) / kDocTile;
   constexpr int smem = fwd2::Cfg<D>::SMEM;
@@ -233,9 +256,9 @@ static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2*
 
 template <int D, bool BF16>
 static int launch_sm100_fwd(const attn_fwd_params_t* p, float* lse, const int2* dq_t, const int2* dkv_t,
-                            cudaStream_t st) {
+                            const int2* djr, cudaStream_t st) {
   if (p->seq_q > fwd::BM) {
-    const int rc = launch_sm100_fwd2<D, BF16>(p, lse, dq_t, dkv_t, st);
+    const int rc = launch_sm100_fwd2<D, BF16>(p, lse, dq_t, dkv_t, djr, st);
     if (rc != ATTN_ERR_UNSUPPORTED) return rc;
   }
   CUtensorMap tq, tk, tv;
@@ -251,7 +274,7 @@ static int launch_sm100_fwd(const attn_fwd_params_t* p, float* lse, const int2* 
   a.out = p->out;
   a.o_s0 = p->o_strides[0]; a.o_s1 = p->o_strides[1]; a.o_s2 = p->o_strides[2];
   a.lse = lse; a.mask = p->mask;
-  a.doc_q_tiles = dq_t; a.doc_kv_tiles = dkv_t;
+  a.doc_q_tiles = dq_t; a.doc_kv_tiles = dkv_t; a.doc_jrange = djr;
   a.nq_doc = (p->seq_q + kDocTile - 1) / kDocTile;
   a.nk_doc = (p->seq_kv + kDocTile - 1) / kDocTile;
   constexpr int smem = fwd::Cfg<D>::SMEM;
@@ -335,27 +358,23 @@ int attn_fwd(const attn_fwd_params_t* p, void* stream) {
 
   const bool tc = tc_layout_ok(p);
   if (!tc && !simt_dim_ok(p->head_dim)) return ATTN_ERR_UNSUPPORTED;
-  int2 *dq_t = nullptr, *dkv_t = nullptr;
+  int2 *dq_t = nullptr, *dkv_t = nullptr, *djr = nullptr;
   if (p->mask.doc_q && tc) {
-    const int nq = (p->seq_q + kDocTile - 1) / kDocTile, nk = (p->seq_kv + kDocTile - 1) / kDocTile;
     dq_t = reinterpret_cast<int2*>(ws + w.doc_q);
     dkv_t = reinterpret_cast<int2*>(ws + w.doc_kv);
-    doc_tile_range_kernel<<<dim3(nq, p->batch), 128, 0, st>>>(p->mask.doc_q, p->mask.doc_q_bstride,
-                                                               p->mask.q_offset, p->seq_q, nq, dq_t);
-    doc_tile_range_kernel<<<dim3(nk, p->batch), 128, 0, st>>>(
-        p->mask.doc_kv, p->mask.doc_kv_bstride, p->mask.kv_offset, p->seq_kv, nk, dkv_t);
-    const int lrc = launch_status(2);
+    djr = reinterpret_cast<int2*>(ws + w.doc_jr);
+    const int lrc = launch_doc_ranges(p->mask, p->batch, p->seq_q, p->seq_kv, dq_t, dkv_t, djr, nullptr, st);
     if (lrc != ATTN_OK) return lrc;
   }
   int rc;
   if (tc) {
     const bool bf = p->dtype == ATTN_BF16;
     if (p->head_dim == 128)
-      rc = bf ? launch_sm100_fwd<128, true>(p, lse, dq_t, dkv_t, st)
-              : launch_sm100_fwd<128, false>(p, lse, dq_t, dkv_t, st);
+      rc = bf ? launch_sm100_fwd<128, true>(p, lse, dq_t, dkv_t, djr, st)
+              : launch_sm100_fwd<128, false>(p, lse, dq_t, dkv_t, djr, st);
     else
-      rc = bf ? launch_sm100_fwd<64, true>(p, lse, dq_t, dkv_t, st)
-              : launch_sm100_fwd<64, false>(p, lse, dq_t, dkv_t, st);
+      rc = bf ? launch_sm100_fwd<64, true>(p, lse, dq_t, dkv_t, djr, st)
+              : launch_sm100_fwd<64, false>(p, lse, dq_t, dkv_t, djr, st);
   } else if (p->dtype == ATTN_F32) {
     rc = launch_simt_fwd<float>(p, lse, st);
   } else if (p->dtype == ATTN_BF16) {
@@ -402,7 +421,7 @@ static int bwd_seq_pad(const attn_bwd_params_t* p) { return (p->seq_q + 127) / 1
 static bool bwd_fused_dq(const attn_bwd_params_t* p) { return ATTN_BWD_FUSED_DQ && p->head_dim == 128; }
 
 struct BwdWorkspace {
-  size_t lse2 = 0, dq_acc = 0, total = 0;  // delta at offset 0
+  size_t lse2 = 0, dq_acc = 0, doc_q = 0, doc_kv = 0, doc_q_jr = 0, doc_kv_qr = 0, total = 0;  // delta at 0
 };
 
 static BwdWorkspace bwd_workspace_layout(const attn_bwd_params_t* p) {
@@ -411,9 +430,25 @@ static BwdWorkspace bwd_workspace_layout(const attn_bwd_params_t* p) {
   const size_t rows = (size_t)p->batch * p->num_heads_q * (tc ? bwd_seq_pad(p) : p->seq_q);
   w.lse2 = align256(rows * sizeof(float));
   w.dq_acc = 2 * w.lse2;
-  w.total = w.dq_acc + ((tc && bwd_fused_dq(p)) ? align256(rows * p->head_dim * sizeof(float)) : 0);
+  size_t off = w.dq_acc + ((tc && bwd_fused_dq(p)) ? align256(rows * p->head_dim * sizeof(float)) : 0);
+  if (tc && p->mask.doc_q) {
+    const size_t nq = (p->seq_q + kDocTile - 1) / kDocTile, nk = (p->seq_kv + kDocTile - 1) / kDocTile;
+    w.doc_q = off;
+    off += align256(p->batch * nq * sizeof(int2));
+    w.doc_kv = off;
+    off += align256(p->batch * nk * sizeof(int2));
+    w.doc_q_jr = off;
+    off += align256(p->batch * nq * sizeof(int2));
+    w.doc_kv_qr = off;
+    off += align256(p->batch * nk * sizeof(int2));
+  }
+  w.total = off;
   return w;
 }
+
+struct BwdDocTables {
+  const int2 *q_t = nullptr, *kv_t = nullptr, *q_jr = nullptr, *kv_qr = nullptr;
+};
 
 // Sets the kernel's dynamic shared-memory limit once per device.
 template <typename K>
@@ -427,7 +462,8 @@ static bool smem_attr_once(K kernel, int bytes, int* cached_dev) {
 }
 
 template <int D, bool BF16>
-static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse2, float* dq_acc, cudaStream_t st) {
+static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse2, float* dq_acc,
+                            const BwdDocTables& doc, cudaStream_t st) {
   using namespace bwd;
   const int Sq_pad = bwd_seq_pad(p);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -449,6 +485,9 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
     a.dq_s[i] = p->dq_strides[i]; a.dk_s[i] = p->dk_strides[i]; a.dv_s[i] = p->dv_strides[i];
   }
   a.mask = p->mask;
+  a.doc_q_tiles = doc.q_t; a.doc_kv_tiles = doc.kv_t; a.doc_q_jr = doc.q_jr; a.doc_kv_qr = doc.kv_qr;
+  a.nq_doc = (p->seq_q + kDocTile - 1) / kDocTile;
+  a.nk_doc = (p->seq_kv + kDocTile - 1) / kDocTile;
   CUtensorMap q64, do64, k128, v128, q128, do128, k64, v64;
   const int B = p->batch, Hq = p->num_heads_q, Hkv = p->num_heads_kv, Sq = p->seq_q, Skv = p->seq_kv;
   if (!make_tmap(&q64, p->dtype, p->q, B, Hq, Sq, D, p->q_strides, QT) ||
@@ -534,13 +573,24 @@ int attn_bwd(const attn_bwd_params_t* p, void* stream) {
 
   if (tc) {
     int rc;
+    BwdDocTables doc;
+    if (p->mask.doc_q) {
+      char* wb = reinterpret_cast<char*>(p->workspace);
+      int2* q_t = reinterpret_cast<int2*>(wb + wl.doc_q);
+      int2* kv_t = reinterpret_cast<int2*>(wb + wl.doc_kv);
+      int2* q_jr = reinterpret_cast<int2*>(wb + wl.doc_q_jr);
+      int2* kv_qr = reinterpret_cast<int2*>(wb + wl.doc_kv_qr);
+      rc = launch_doc_ranges(p->mask, p->batch, p->seq_q, p->seq_kv, q_t, kv_t, q_jr, kv_qr, st);
+      if (rc != ATTN_OK) return rc;
+      doc.q_t = q_t; doc.kv_t = kv_t; doc.q_jr = q_jr; doc.kv_qr = kv_qr;
+    }
     const bool bf = p->dtype == ATTN_BF16;
     if (p->head_dim == 128)
-      rc = bf ? launch_sm100_bwd<128, true>(p, delta, lse2, dq_acc, st)
-              : launch_sm100_bwd<128, false>(p, delta, lse2, dq_acc, st);
+      rc = bf ? launch_sm100_bwd<128, true>(p, delta, lse2, dq_acc, doc, st)
+              : launch_sm100_bwd<128, false>(p, delta, lse2, dq_acc, doc, st);
     else
-      rc = bf ? launch_sm100_bwd<64, true>(p, delta, lse2, dq_acc, st)
-              : launch_sm100_bwd<64, false>(p, delta, lse2, dq_acc, st);
+      rc = bf ? launch_sm100_bwd<64, true>(p, delta, lse2, dq_acc, doc, st)
+              : launch_sm100_bwd<64, false>(p, delta, lse2, dq_acc, doc, st);
     if (rc != ATTN_OK || !p->fix_masked_rows) return rc;
     auto fix = [&](auto tag) {
       using T = decltype(tag);

@@ -89,6 +89,14 @@ struct Args {
   float* dq_acc;       // fused dQ: [B][Hq][Sq_pad][D] fp32, zeroed before the kernel
   long long dq_s[3], dk_s[3], dv_s[3];
   attn_mask_t mask;
+  // Document masks: (min, max) ids per kDocTile tile of q / kv, and the
+  // overlapping tile range of the other side per q tile (q_jr) / kv tile
+  // (kv_qr), all in kDocTile units (null without a document mask).
+  const int2* doc_q_tiles;
+  const int2* doc_kv_tiles;
+  const int2* doc_q_jr;
+  const int2* doc_kv_qr;
+  int nq_doc, nk_doc;
 };
 
 // q-tile index range [lo, hi) (tiles of QT) that the band allows for kv rows [k0, k1).
@@ -215,11 +223,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int t_lo, t_hi;
   band_q_range(a.mask, k0, k1, a.Sq, &t_lo, &t_hi);
+  if (a.doc_kv_qr) {
+    static_assert(KROWS == kDocTile && kDocTile % QT == 0, "document tiles vs kv / q tiles");
+    const int2 r = a.doc_kv_qr[(long long)b * a.nk_doc + kt];
+    t_lo = max(t_lo, r.x * (kDocTile / QT));
+    t_hi = max(t_lo, min(t_hi, r.y * (kDocTile / QT)));
+  }
   const int ntiles = t_hi - t_lo;
   const int iters = a.group * ntiles;  // (g, q tile) pairs, g outer
   auto state_of = [&](int qt) {
     const int q0 = qt * QT;
-    return tile_state(a.mask, nullptr, nullptr, 0, 0, b, q0, min(q0 + QT, a.Sq), k0, k1, KROWS);
+    return tile_state(a.mask, a.doc_q_tiles, a.doc_kv_tiles, a.nq_doc, a.nk_doc, b, q0, min(q0 + QT, a.Sq), k0,
+                      k1, KROWS);
   };
   // Inside [t_lo, t_hi) only a prefix mask (or a document mask) can drop a
   // whole tile; the TMA and MMA warps classify tiles only then.
@@ -643,8 +658,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int j_lo, j_hi;
   band_tile_range(a.mask, q0, q1, a.Skv, KT, &j_lo, &j_hi);
+  if (a.doc_q_jr) {
+    static_assert(QROWS == kDocTile && kDocTile % KT == 0, "document tiles vs q / kv tiles");
+    const int2 r = a.doc_q_jr[(long long)b * a.nq_doc + qt];
+    j_lo = max(j_lo, r.x * (kDocTile / KT));
+    j_hi = max(j_lo, min(j_hi, r.y * (kDocTile / KT)));
+  }
   auto state_of = [&](int j) {
-    return tile_state(a.mask, nullptr, nullptr, 0, 0, b, q0, q1, j * KT, min((j + 1) * KT, a.Skv), KT);
+    return tile_state(a.mask, a.doc_q_tiles, a.doc_kv_tiles, a.nq_doc, a.nk_doc, b, q0, q1, j * KT,
+                      min((j + 1) * KT, a.Skv), KT);
   };
 
   if (warp == 8) {

@@ -78,6 +78,7 @@ struct Args {
   attn_mask_t mask;
   const int2* doc_q_tiles;
   const int2* doc_kv_tiles;
+  const int2* doc_jrange;  // per q tile: kv tiles whose document ids can match (or null)
   int nq_doc, nk_doc;
 };
 
@@ -151,6 +152,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int x = 0; x < 2; ++x) {
     if (act[x]) band_tile_range(a.mask, q0[x], q1[x], a.Skv, BN, &jl[x], &jh[x]);
     else jl[x] = jh[x] = 0;
+    if (act[x] && a.doc_jrange) {
+      const int2 r = a.doc_jrange[(long long)b * a.nq_doc + q0[x] / kDocTile];
+      jl[x] = max(jl[x], r.x);
+      jh[x] = max(jl[x], min(jh[x], r.y));
+    }
   }
   const int j_lo = act[1] ? min(jl[0], jl[1]) : jl[0];
   const int j_hi = act[1] ? max(jh[0], jh[1]) : jh[0];

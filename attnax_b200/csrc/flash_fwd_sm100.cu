@@ -54,6 +54,7 @@ struct Args {
   attn_mask_t mask;
   const int2* doc_q_tiles;
   const int2* doc_kv_tiles;
+  const int2* doc_jrange;  // per q tile: kv tiles whose document ids can match (or null)
   int nq_doc, nk_doc;
 };
 
@@ -111,6 +112,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int j_lo, j_hi;
   band_tile_range(a.mask, q0, q1, a.Skv, BN, &j_lo, &j_hi);
+  if (a.doc_jrange) {
+    static_assert(BM == kDocTile, "one document tile per q tile");
+    const int2 r = a.doc_jrange[(long long)b * a.nq_doc + q0 / kDocTile];
+    j_lo = max(j_lo, r.x);
+    j_hi = max(j_lo, min(j_hi, r.y));
+  }
   auto state_of = [&](int j) {
     return tile_state(a.mask, a.doc_q_tiles, a.doc_kv_tiles, a.nq_doc, a.nk_doc, b, q0, q1, j * BN,
                       min((j + 1) * BN, a.Skv), BN);
