@@ -389,7 +389,7 @@ def run_paged(args, torch, peaks):
 def run_document(args, torch, peaks):
     import attnax_b200 as ax
     from attnax_b200._spec import build_spec
-    from attnax_b200.flash import fwd_raw
+    from attnax_b200.flash import bwd_raw, fwd_raw
 
     S = 32768 if args.scale == "full" else 8192
     H, D = 16, 128
@@ -406,8 +406,14 @@ def run_document(args, torch, peaks):
     pairs = sum(L * (L + 1) // 2 for L in lens)
     fl = 4.0 * D * H * pairs
     tf = fl / (ms * 1e-3) / 1e12
+    # backward of the same call (P recomputed from the forward LSE)
+    do = torch.randn(1, H, S, D, generator=g, device=dev).to(torch.bfloat16)
+    o2, lse = fwd_raw(q, k, v, spec)
+    ms_b, _ = tm.run(lambda m: bwd_raw(q, k, v, o2, lse, do, spec), args.steps, args.warmup)
+    tf_b = 2.5 * fl / (ms_b * 1e-3) / 1e12
     return {"metric": "document-mask flash fwd TFLOP/s (algorithmic)", "value": round(tf, 2),
             "unit": "TFLOP/s", "ms_per_step": round(ms, 4), "docs": len(lens), "pairs": pairs,
+            "bwd_tflops": round(tf_b, 2), "bwd_ms": round(ms_b, 4),
             "config": f"B1 S{S} H{H} D{D} bf16 document_mask+causal",
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4)}}
@@ -441,9 +447,20 @@ def run_ring(args, torch, dist, rank, world, peaks):
     ms, _ = tm.run(step, steps, 3)
     fl = 4.0 * D * Hq * S * (S + 1) / 2
     tf = fl / (ms * 1e-3) / 1e12
+    # Per-GPU reference for the ring: one GPU's causal flash forward on a
+    # sequence of the shard length S/P (same heads), no exchange.
+    base = None
+    if world > 1:
+        if rank == 0:
+            t1 = Timer(torch, None, 1)
+            with torch.no_grad():
+                b_ms, _ = t1.run(lambda m: ax.flash_attention(q, k, v, score_mod=mod), steps, 3)
+            base = round(4.0 * D * Hq * Sl * (Sl + 1) / 2 / (b_ms * 1e-3) / 1e12, 2)
+        dist.barrier()
     return {"metric": "ring attention tokens/s", "value": round(S / (ms * 1e-3), 1), "unit": "tokens/s",
             "n_gpus": world, "ms_per_step": round(ms, 3), "tflops_total": round(tf, 2),
-            "tflops_per_gpu": round(tf / world, 2), "scaling": "strong",
+            "tflops_per_gpu": round(tf / world, 2), "one_gpu_causal_tflops_at_shard_len": base,
+            "scaling": "strong",
             "config": f"B1 S{S} (S/P={Sl}) Hq{Hq} Hkv{Hkv} D{D} bf16 causal, "
                       f"{'zig-zag ring over NCCL' if world > 1 else 'one GPU, flash kernel'}"}
 
