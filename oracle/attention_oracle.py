@@ -28,7 +28,8 @@ __all__ = [
     "repeat_kv", "gqa_attention", "gqa_attention_bwd",
     "ring_attention_partitioned", "PagedKVCache", "init_paged_kv_cache",
     "allocate_blocks", "append_kv", "gather_kv", "paged_attention",
-    "paged_attention_batched", "softmax_scale", "bf16_round",
+    "paged_attention_batched", "softmax_scale", "bf16_round", "KVLayerCache",
+    "init_kv_layer_cache", "update_kv_layer_cache", "kv_cache_attention",
 ]
 
 
@@ -595,3 +596,46 @@ def paged_attention(query, cache, sequence_idx, *, mask=None, score_mod=None):
 def paged_attention_batched(query, cache):
     """``paged_attention`` for every sequence: ``query`` is ``(B, Hq, Sq, D)``."""
     return np.stack([paged_attention(query[i], cache, i) for i in range(query.shape[0])])
+
+
+# ----------------------------------------------------------------------------
+# cache.py: the contiguous per-layer KV cache used for decoding
+# ----------------------------------------------------------------------------
+
+@dataclass
+class KVLayerCache:
+    """``keys``/``values`` ``(B, Hkv, max_len, D)`` + scalar ``length`` (cache.py:15-36)."""
+
+    keys: np.ndarray
+    values: np.ndarray
+    length: int
+
+    @property
+    def max_len(self):
+        return int(self.keys.shape[2])
+
+
+def init_kv_layer_cache(batch_size, num_kv_heads, head_dim, max_len, dtype=np.float32):
+    """Zero buffers, length 0 (cache.py:39-64)."""
+    z = np.zeros((batch_size, num_kv_heads, max_len, head_dim), dtype=dtype)
+    return KVLayerCache(z, z.copy(), 0)
+
+
+def update_kv_layer_cache(cache, keys_new, values_new, start):
+    """Writes ``[start, start + chunk)`` and sets ``length = start + chunk``;
+    ``ValueError`` past ``max_len`` (cache.py:67-98)."""
+    end = start + keys_new.shape[2]
+    if end > cache.max_len:
+        raise ValueError(f"KV cache overflow: end={end} exceeds max_len={cache.max_len}")
+    k, v = cache.keys.copy(), cache.values.copy()
+    k[:, :, start:end] = keys_new
+    v[:, :, start:end] = values_new
+    return KVLayerCache(k, v, end)
+
+
+def kv_cache_attention(query, cache, *, mask=None, score_mod=None):
+    """``query (B, Hq, Sq, D)`` over the cache's first ``length`` positions with
+    kv heads repeated -- what ``MultiHeadAttention`` computes from the
+    concatenated history (attnax/attention.py:386-400, :32-39)."""
+    n = int(cache.length)
+    return gqa_attention(query, cache.keys[:, :, :n], cache.values[:, :, :n], mask=mask, score_mod=score_mod)

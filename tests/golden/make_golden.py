@@ -36,6 +36,40 @@ def load_reference(ref_root: pathlib.Path):
     return K, M, PC
 
 
+def make_kvcache(ref_root: pathlib.Path, K):
+    """Contiguous per-layer KV cache (``attnax/cache.py``): a prefill chunk and a
+    decode token written with ``update_kv_layer_cache``, the overflow error,
+    and attention of the decode queries over ``keys[:, :, :length]`` (what
+    ``MultiHeadAttention`` computes from the concatenated history,
+    ``attnax/attention.py:386-400``)."""
+    import attnax.cache as KC  # noqa: E402
+    out = {}
+    rng = np.random.default_rng(6)
+    B, Hq, Hkv, L, D = 2, 4, 2, 40, 16
+    c = KC.init_kv_layer_cache(B, Hkv, D, L, np.float32)
+    out["kvc_init_len"] = np.asarray(c.length)
+    k1, v1 = rnd(rng, (B, Hkv, 13, D)), rnd(rng, (B, Hkv, 13, D))
+    c = KC.update_kv_layer_cache(c, A(k1), A(v1), 0)
+    k2, v2 = rnd(rng, (B, Hkv, 1, D)), rnd(rng, (B, Hkv, 1, D))
+    c = KC.update_kv_layer_cache(c, A(k2), A(v2), int(c.length))
+    out.update(kvc_k1=k1, kvc_v1=v1, kvc_k2=k2, kvc_v2=v2, kvc_keys=np.asarray(c.keys),
+               kvc_values=np.asarray(c.values), kvc_len=np.asarray(c.length))
+    try:
+        KC.update_kv_layer_cache(c, A(rnd(rng, (B, Hkv, 27, D))), A(rnd(rng, (B, Hkv, 27, D))), int(c.length))
+        out["kvc_overflow_raises"] = np.array(0)
+    except ValueError:
+        out["kvc_overflow_raises"] = np.array(1)
+    n = int(c.length)
+    for sq in (1, 3):
+        q = rnd(rng, (B, Hq, sq, D))
+        out[f"kvc_q{sq}"] = q
+        # the MHA repeats kv heads before attention (_repeat_kv_heads, attnax/attention.py:32-39)
+        kr = A(np.repeat(np.asarray(c.keys[:, :, :n, :]), Hq // Hkv, axis=1))
+        vr = A(np.repeat(np.asarray(c.values[:, :, :n, :]), Hq // Hkv, axis=1))
+        out[f"kvc_out{sq}"] = np.asarray(K.standard_attention(A(q), kr, vr))
+    np.savez_compressed(HERE / "golden_kvcache.npz", **out)
+
+
 def rnd(rng, shape, bf16=False):
     x = rng.standard_normal(shape, dtype=np.float32)
     if bf16:
@@ -52,8 +86,14 @@ def A(x):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", choices=["kvcache"], default=None,
+                    help="write only this fixture (leaves the other files untouched)")
     args = ap.parse_args()
     K, M, PC = load_reference(pathlib.Path(args.ref))
+    if args.only == "kvcache":
+        make_kvcache(pathlib.Path(args.ref), K)
+        print("golden_kvcache.npz written to", HERE)
+        return
     out = {}
 
     # --- score-mod chains through standard_attention ---------------------
@@ -206,6 +246,7 @@ def main():
                                                                    score_mod=K.causal_mod()))
     out["ring_unbound"] = np.asarray(K.ring_attention(A(q), A(k), A(v), axis_name="not_bound"))
     np.savez_compressed(HERE / "golden_ring.npz", **out)
+    make_kvcache(pathlib.Path(args.ref), K)
     print("golden vectors written to", HERE)
 
 

@@ -157,6 +157,47 @@ def test_ring_partitioned_matches_bound_axis_golden(P, name):
     np.testing.assert_allclose(out, ref, atol=1e-5, rtol=1e-5)
 
 
+def test_kv_layer_cache_golden():
+    """Contiguous KV cache (cache.py): updates bit-exact, overflow raises,
+    decode attention over the first ``length`` positions."""
+    d = load("kvcache")
+    B, Hkv, _, D = d["kvc_k1"].shape
+    c = O.init_kv_layer_cache(B, Hkv, D, d["kvc_keys"].shape[2])
+    assert c.length == int(d["kvc_init_len"]) == 0
+    c = O.update_kv_layer_cache(c, d["kvc_k1"], d["kvc_v1"], 0)
+    c = O.update_kv_layer_cache(c, d["kvc_k2"], d["kvc_v2"], c.length)
+    assert c.length == int(d["kvc_len"])
+    np.testing.assert_array_equal(c.keys, d["kvc_keys"])
+    np.testing.assert_array_equal(c.values, d["kvc_values"])
+    assert int(d["kvc_overflow_raises"]) == 1
+    with pytest.raises(ValueError, match="overflow"):
+        O.update_kv_layer_cache(c, np.zeros((B, Hkv, 27, D), np.float32), np.zeros((B, Hkv, 27, D), np.float32),
+                                c.length)
+    for sq in (1, 3):
+        np.testing.assert_allclose(O.kv_cache_attention(d[f"kvc_q{sq}"], c), d[f"kvc_out{sq}"], atol=1e-6)
+
+
+def test_kv_layer_cache_update_host_logic_golden():
+    """The library's update (a device copy into the buffers; here on host
+    tensors) reproduces the reference's cache contents bit for bit."""
+    import torch
+
+    import attnax_b200 as ax
+
+    d = load("kvcache")
+    B, Hkv, _, D = d["kvc_k1"].shape
+    c = ax.init_kv_layer_cache(B, Hkv, D, d["kvc_keys"].shape[2], torch.float32, device="cpu")
+    c = ax.update_kv_layer_cache(c, torch.from_numpy(d["kvc_k1"]), torch.from_numpy(d["kvc_v1"]), 0)
+    c = ax.update_kv_layer_cache(c, torch.from_numpy(d["kvc_k2"]), torch.from_numpy(d["kvc_v2"]), c.length)
+    assert c.length == int(d["kvc_len"])
+    np.testing.assert_array_equal(c.keys.numpy(), d["kvc_keys"])
+    np.testing.assert_array_equal(c.values.numpy(), d["kvc_values"])
+    with pytest.raises(ValueError, match="overflow"):
+        ax.update_kv_layer_cache(c, torch.zeros(B, Hkv, 27, D), torch.zeros(B, Hkv, 27, D), c.length)
+    assert len(ax.init_decoder_kv_caches(num_layers=3, batch_size=1, num_kv_heads=2, head_dim=8, max_len=4,
+                                         dtype=torch.float32, device="cpu")) == 3
+
+
 def test_ring_unbound_axis_falls_back_golden():
     d = load("ring")
     out = O.standard_attention(d["ring_q"], d["ring_k"], d["ring_v"])
