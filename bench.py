@@ -386,6 +386,35 @@ def run_paged(args, torch, peaks):
             "gpu_launches": int(launches)}
 
 
+def run_kv_cache(args, torch, peaks):
+    """Decode step over the contiguous per-layer KV cache: batch 32, Hq32 Hkv8
+    D128 bf16, 16000 of 16384 positions filled, one query position."""
+    import attnax_b200 as ax
+    from attnax_b200 import _lib
+
+    B, Hq, Hkv, D = (32, 32, 8, 128) if args.scale == "full" else (8, 32, 8, 128)
+    L, n = 16384, 16000
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(9)
+    cache = ax.init_kv_layer_cache(B, Hkv, D, L, torch.bfloat16)
+    cache = ax.update_kv_layer_cache(cache, torch.randn(B, Hkv, n, D, generator=g, device=dev).to(torch.bfloat16),
+                                     torch.randn(B, Hkv, n, D, generator=g, device=dev).to(torch.bfloat16), 0)
+    q = torch.randn(B, Hq, 1, D, generator=g, device=dev).to(torch.bfloat16)
+    tm = Timer(torch, None, 1)
+    lib = _lib.load()
+    n0 = lib.attn_launch_count()
+    ms, _ = tm.run(lambda m: ax.kv_cache_attention(q, cache), args.steps * 5, args.warmup)
+    launches = (lib.attn_launch_count() - n0) * args.steps * 5 // (args.steps * 5 + args.warmup)
+    alg_bytes = 2 * B * Hkv * n * D * 2 + 2 * q.numel() * 2
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    return {"metric": "KV-cache decode HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "algorithmic_bytes": alg_bytes,
+            "config": f"B{B} Hq{Hq} Hkv{Hkv} D{D} bf16, {n} of {L} cached positions, one query position",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4)},
+            "gpu_launches": int(launches)}
+
+
 def run_document(args, torch, peaks):
     import attnax_b200 as ax
     from attnax_b200._spec import build_spec
@@ -544,7 +573,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["flash", "paged", "document", "fp32", "ring"], default="flash")
+    ap.add_argument("--workload", choices=["flash", "paged", "kv_cache", "document", "fp32", "ring"],
+                    default="flash")
     ap.add_argument("--scale", choices=["full", "small"], default="full")
     ap.add_argument("--no-secondary", action="store_true")
     args = ap.parse_args()
@@ -595,12 +625,15 @@ def main():
             ring = None if args.no_secondary else run_ring(args, torch, dist, rank, world, peaks)
             if rank == 0 and not args.no_secondary:
                 line["secondary"] = {"ring": ring, "paged": run_paged(args, torch, peaks),
+                                     "kv_cache": run_kv_cache(args, torch, peaks),
                                      "document": run_document(args, torch, peaks),
                                      "fp32": run_fp32(args, torch, peaks)}
             if world > 1:
                 dist.barrier()
         elif args.workload == "paged":
             line = run_paged(args, torch, peaks)
+        elif args.workload == "kv_cache":
+            line = run_kv_cache(args, torch, peaks)
         elif args.workload == "document":
             line = run_document(args, torch, peaks)
         elif args.workload == "ring":
