@@ -110,11 +110,13 @@ def redeal(sched: RingSchedule, ops, tensors, to_work: bool):
     return outs
 
 
-def ring_schedule_forward(q, k, v, *, ops, sched: RingSchedule, band):
+def ring_schedule_forward(q, k, v, *, ops, sched: RingSchedule, band, state=None):
     """Runs the ring; returns the local output shard in the public layout.
 
     ``band``: (lo, hi) of the causal/window selection, used to skip chunk
     pairs with nothing kept (the kernel would return an empty partial).
+    ``state``: if a dict, receives what the backward needs, in the ring
+    layout: ``q``, ``k``, ``v``, the output ``out`` and the merged ``lse``.
     """
     P, r, C = sched.P, sched.r, sched.C
     if sched.zigzag:
@@ -141,9 +143,67 @@ def ring_schedule_forward(q, k, v, *, ops, sched: RingSchedule, band):
             kv = ops.finish_rotate(nxt)
     outs = [ops.finalize(a, q_parts[0].dtype) for a in acc]
     out = torch.cat(outs, dim=2) if len(outs) > 1 else outs[0]
+    if state is not None:
+        state.update(q=q, k=k.contiguous(), v=v.contiguous(), out=out,
+                     lse=torch.cat([a[1] for a in acc], dim=2) if len(acc) > 1 else acc[0][1])
     if sched.zigzag:
         (out,) = redeal(sched, ops, [out], to_work=False)
     return out, acc
+
+
+def ring_schedule_backward(q, k, v, out, lse, dout, *, ops, sched: RingSchedule, band, empty_rows=False):
+    """Gradients of the ring for this rank's shards.
+
+    ``q``, ``k``, ``v``, ``out``, ``lse`` are in the ring layout (as the
+    forward left them in ``state``), ``dout`` in the public layout.  The K/V
+    shards travel the ring again; at every hop each kept (q chunk, kv chunk)
+    pair gives exact partial gradients from the global ``lse`` and
+    ``rowsum(dout * out)`` (the softmax of the whole row), dQ accumulates
+    here and dK/dV accumulate in fp32 buffers that travel with their K/V --
+    one rotation per hop brings every rank's own dK/dV home after the last
+    hop.  ``empty_rows``: rows with no kept key anywhere (lse = -inf) get the
+    reference's uniform-softmax term, dV += dout / S_global for every key
+    (one all-reduce; their dQ and dK are zero).  Returns fp32
+    ``(dq, dk, dv)`` in the public layout.
+    """
+    P, r, C = sched.P, sched.r, sched.C
+    if sched.zigzag:
+        (dout,) = redeal(sched, ops, [dout], to_work=True)
+    my_chunks = [sched.chunk(c) for c in sched.held(r)]
+    q_parts = torch.split(q, C, dim=2)
+    o_parts = torch.split(out, C, dim=2)
+    do_parts = torch.split(dout, C, dim=2)
+    lse_parts = torch.split(lse, C, dim=2)
+    dq = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+    dq_parts = torch.split(dq, C, dim=2)
+    kv = (k, v)
+    dkv = (torch.zeros(k.shape, dtype=torch.float32, device=k.device),
+           torch.zeros(v.shape, dtype=torch.float32, device=v.device))
+    for i in range(P):
+        owner = (r - i) % P
+        nxt = ops.start_rotate(kv, to=(r + 1) % P, frm=(r - 1) % P) if i < P - 1 else None
+        kv_chunks = [sched.chunk(c) for c in sched.held(owner)]
+        k_parts, v_parts = torch.split(kv[0], C, dim=2), torch.split(kv[1], C, dim=2)
+        dk_parts, dv_parts = torch.split(dkv[0], C, dim=2), torch.split(dkv[1], C, dim=2)
+        for qi, qc in enumerate(my_chunks):
+            for ki, kc in enumerate(kv_chunks):
+                if _pairs_all_masked(band, qc.start, kc.start, C):
+                    continue
+                gq, gk, gv = ops.grad(q_parts[qi], k_parts[ki], v_parts[ki], o_parts[qi], lse_parts[qi],
+                                      do_parts[qi], qc, kc)
+                dq_parts[qi].add_(gq)
+                dk_parts[ki].add_(gk)
+                dv_parts[ki].add_(gv)
+        # the accumulators follow their K/V: after hop i rank r holds owner (r - i - 1)'s
+        dkv = ops.finish_rotate(ops.start_rotate(dkv, to=(r + 1) % P, frm=(r - 1) % P))
+        if nxt is not None:
+            kv = ops.finish_rotate(nxt)
+    dk, dv = dkv
+    if empty_rows:
+        dv = dv + ops.empty_rows_dv(dout, lse, k.shape[1], C * sched.nchunks)[:, :, None, :]
+    if sched.zigzag:
+        dq, dk, dv = redeal(sched, ops, [dq, dk, dv], to_work=False)
+    return dq, dk, dv
 
 
 class DistExchange:
@@ -162,19 +222,28 @@ class DistExchange:
             for w in dist.batch_isend_irecv(ops):
                 w.wait()
 
-    def start_rotate(self, kv, to, frm):
-        nk, nv = torch.empty_like(kv[0]), torch.empty_like(kv[1])
-        ops = [dist.P2POp(dist.isend, kv[0], self._peer(to), self.group),
-               dist.P2POp(dist.isend, kv[1], self._peer(to), self.group),
-               dist.P2POp(dist.irecv, nk, self._peer(frm), self.group),
-               dist.P2POp(dist.irecv, nv, self._peer(frm), self.group)]
-        return dist.batch_isend_irecv(ops), (nk, nv)
+    def start_rotate(self, ts, to, frm):
+        """Sends every tensor of ``ts`` to ``to`` and receives same-shaped ones from ``frm``."""
+        new = tuple(torch.empty_like(t) for t in ts)
+        ops = [dist.P2POp(dist.isend, t, self._peer(to), self.group) for t in ts]
+        ops += [dist.P2POp(dist.irecv, t, self._peer(frm), self.group) for t in new]
+        return dist.batch_isend_irecv(ops), new
 
     def finish_rotate(self, pending):
         works, kv = pending
         for w in works:
             w.wait()
         return kv
+
+    def empty_rows_dv(self, dout, lse, heads_kv, n_global):
+        """sum over this rank's rows with lse = -inf of dout, per kv head, summed
+        over the ranks and divided by the global sequence length: (B, Hkv, D)."""
+        B, Hq, _, D = dout.shape
+        keep = (lse == float("-inf")).to(torch.float32 if dout.dtype != torch.float64 else torch.float64)
+        s = (dout.to(keep.dtype) * keep[..., None]).sum(dim=2)
+        s = s.view(B, heads_kv, Hq // heads_kv, D).sum(dim=2)
+        dist.all_reduce(s, group=self.group)
+        return s / n_global
 
 
 class KernelOps(DistExchange):
@@ -202,9 +271,8 @@ class KernelOps(DistExchange):
             t = t[..., kc.local_start:kc.local_start + n]
         return t
 
-    def attend(self, q, k, v, qc, kc):
+    def _spec(self, q, k, qc, kc):
         from ._spec import build_spec
-        from .flash import fwd_raw
         from .score_mods import AdditiveBiasMod
         from ._spec import flatten_mods
         from ._api import compose_score_mods
@@ -218,7 +286,20 @@ class KernelOps(DistExchange):
                           heads_q=self.heads_q, seq_q=n, seq_kv=k.shape[2], device=self.device,
                           q_offset=qc.start, kv_offset=kc.start)
         spec.fix_masked_rows = False  # an empty partial must stay empty (lse = -inf)
-        return fwd_raw(q.contiguous(), k.contiguous(), v.contiguous(), spec)
+        return spec
+
+    def attend(self, q, k, v, qc, kc):
+        from .flash import fwd_raw
+
+        return fwd_raw(q.contiguous(), k.contiguous(), v.contiguous(), self._spec(q, k, qc, kc))
+
+    def grad(self, q, k, v, o, lse, do, qc, kc):
+        """Partial (dq, dk, dv) of one chunk pair from the global lse (rows with no
+        key anywhere have lse = -inf: P = 0, their dV term is added by the caller)."""
+        from .flash import bwd_raw
+
+        return bwd_raw(q.contiguous(), k.contiguous(), v.contiguous(), o.contiguous(), lse.contiguous(),
+                       do.contiguous(), self._spec(q, k, qc, kc))
 
     def merge(self, acc, o_p, lse_p):
         import ctypes as C

@@ -9,6 +9,8 @@ names fall back to the local flash kernel the same way.
 
 from __future__ import annotations
 
+import torch
+
 from .flash import _output_dropout, attention
 
 _AXES = {}
@@ -45,20 +47,29 @@ def ring_forward(query, key, value, *, mask=None, score_mod=None, group=None, zi
     rank's contiguous shard of the global sequence; returns this rank's
     output shard.  ``mask`` (and an additive bias) are local
     ``(.., S, S)`` tensors applied at every step, as in the reference
-    (attention.py:659-660).  Forward only.
+    (attention.py:659-660).  Differentiable in ``query``/``key``/``value``:
+    the backward runs the ring again (``ring_schedule_backward``), where the
+    reference differentiates its ``lax.scan``/``ppermute`` with JAX autodiff.
     """
     import torch
-    import torch.distributed as dist
 
-    from ._ring_impl import KernelOps, RingSchedule, ring_schedule_forward
-    from ._spec import band_of, may_empty_rows
     from .flash import check_qkv
 
     B, Hq, Hkv, S, Skv, D = check_qkv(query, key, value)
     if S != Skv:
         raise ValueError("ring_attention needs equal local query and key/value shard lengths")
     if torch.is_grad_enabled() and (query.requires_grad or key.requires_grad or value.requires_grad):
-        raise NotImplementedError("ring_attention backward is not implemented; call it under no_grad")
+        return _RingFn.apply(query, key, value, score_mod, mask, group, zigzag)
+    return _ring_run(query, key, value, score_mod, mask, group, zigzag, None)
+
+
+def _ring_run(query, key, value, score_mod, mask, group, zigzag, state):
+    import torch.distributed as dist
+
+    from ._ring_impl import KernelOps, RingSchedule, ring_schedule_forward
+    from ._spec import band_of, may_empty_rows
+
+    B, Hq, S = query.shape[0], query.shape[1], query.shape[2]
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     band = band_of(score_mod)
     if zigzag is None:
@@ -66,10 +77,34 @@ def ring_forward(query, key, value, *, mask=None, score_mod=None, group=None, zi
     sched = RingSchedule(world, rank, S, zigzag)
     ops = KernelOps(group, score_mod, mask, B, Hq, S, query.device)
     out, acc = ring_schedule_forward(query.contiguous(), key.contiguous(), value.contiguous(),
-                                     ops=ops, sched=sched, band=band)
-    if may_empty_rows(score_mod, mask):
+                                     ops=ops, sched=sched, band=band, state=state)
+    empty = may_empty_rows(score_mod, mask)
+    if empty:
         out = _fill_empty_rows(out, sched, acc, value, group)
+    if state is not None:
+        state.update(sched=sched, ops=ops, band=band, empty=empty)
     return out
+
+
+class _RingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, score_mod, mask, group, zigzag):
+        st = {}
+        out = _ring_run(q, k, v, score_mod, mask, group, zigzag, st)
+        ctx.st, ctx.dtypes = st, (q.dtype, k.dtype, v.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        from ._ring_impl import ring_schedule_backward
+
+        st = ctx.st
+        dq, dk, dv = ring_schedule_backward(st["q"], st["k"], st["v"], st["out"], st["lse"],
+                                            dout.to(st["q"].dtype).contiguous(), ops=st["ops"],
+                                            sched=st["sched"], band=st["band"], empty_rows=st["empty"])
+        ctx.st = None
+        tq, tk, tv = ctx.dtypes
+        return dq.to(tq), dk.to(tk), dv.to(tv), None, None, None, None
 
 
 def _fill_empty_rows(out, sched, acc, value, group):

@@ -62,6 +62,30 @@ class OracleOps:
         lse[empty] = -np.inf
         return torch.from_numpy(o), torch.from_numpy(lse)
 
+    def grad(self, q, k, v, o, lse, do, qc, kc):
+        """Partial (dq, dk, dv) of one chunk pair from the global lse:
+        P = exp(s - lse), dS = P (dP - rowsum(dO o)), zero where the score
+        was dropped (the reference's ``where`` blocks the gradient)."""
+        n, D = q.shape[2], q.shape[3]
+        qn, kn, vn, on, dn = (t.double().numpy() for t in (q, k, v, o, do))
+        ln = lse.double().numpy()[..., None]
+        kr, vr = np.repeat(kn, self.rep, 1), np.repeat(vn, self.rep, 1)
+        m = None
+        if self.mask is not None:
+            m = self.mask[..., qc.local_start:qc.local_start + n, kc.local_start:kc.local_start + n]
+        s = O.attention_oracle._final_scores(qn, kr, m, self.mod, qc.start, kc.start)
+        keep = s != np.finfo(s.dtype).min
+        with np.errstate(over="ignore", invalid="ignore"):
+            p = np.where(np.isinf(ln), 0.0, np.exp(s - ln))
+        dv = np.einsum("bhqk,bhqd->bhkd", p, dn)
+        dp = np.einsum("bhqd,bhkd->bhqk", dn, vr)
+        ds = np.where(keep, p * (dp - (dn * on).sum(-1, keepdims=True)), 0.0)
+        sc = O.softmax_scale(D, np.float64)
+        dq = np.einsum("bhqk,bhkd->bhqd", ds, kr) * sc
+        dk = np.einsum("bhqk,bhqd->bhkd", ds, qn) * sc
+        fold = lambda x: x.reshape(x.shape[0], -1, self.rep, *x.shape[2:]).sum(2)  # noqa: E731
+        return torch.from_numpy(dq), torch.from_numpy(fold(dk)), torch.from_numpy(fold(dv))
+
     def merge(self, acc, o_p, lse_p):
         o_a, l_a = acc
         m = torch.maximum(l_a, lse_p)
@@ -110,6 +134,55 @@ def _worker(rank, world, port, q, k, v, want):
                                        err_msg=case)
     finally:
         dist.destroy_process_group()
+
+
+def _bwd_worker(rank, world, port, q, k, v, do, want):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from attnax_b200._ring_impl import RingSchedule, ring_schedule_backward, ring_schedule_forward
+
+        S = q.shape[2] // world
+        sl = slice(rank * S, (rank + 1) * S)
+        H = q.shape[1]
+        for case in ("none", "causal", "causal_alibi_window"):
+            mod, band, zig = None, None, False
+            if case == "causal":
+                mod, band, zig = O.causal_mod(), (0, 1 << 62), True
+            elif case == "causal_alibi_window":
+                mod = O.compose_score_mods(O.sliding_window_mod(S // 2 + 3), O.alibi_mod(H))
+                band, zig = (0, S // 2 + 2), True
+            sched = RingSchedule(world, rank, S, zig)
+            ops = OracleOps(None, mod, None, q.shape[1], k.shape[1])
+            tq, tk, tv, tdo = (torch.from_numpy(np.ascontiguousarray(x[:, :, sl])).double() for x in (q, k, v, do))
+            st = {}
+            ring_schedule_forward(tq, tk, tv, ops=ops, sched=sched, band=band, state=st)
+            dq, dk, dv = ring_schedule_backward(st["q"], st["k"], st["v"], st["out"], st["lse"], tdo, ops=ops,
+                                                sched=sched, band=band)
+            for name, got, w in zip(("dq", "dk", "dv"), (dq, dk, dv), want[case]):
+                # (1e-6: the oracle's closed-form backward rounds the scale to float32)
+                np.testing.assert_allclose(got.numpy(), w[:, :, sl], atol=1e-6, rtol=1e-6,
+                                           err_msg=f"{case} {name}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ring_backward_schedule_matches_global_gradients(world):
+    """dK/dV travel with their K/V and come home after P hops; every rank's
+    gradient shards equal the global attention's gradients."""
+    rng = np.random.default_rng(10 + world)
+    B, Hq, Hkv, S, D = 1, 4, 2, 16 * world, 8
+    q, k, v, do = (rng.standard_normal((B, h, S, D)) for h in (Hq, Hkv, Hkv, Hq))
+    Sl = S // world
+    want = {
+        "none": O.gqa_attention_bwd(q, k, v, do),
+        "causal": O.gqa_attention_bwd(q, k, v, do, score_mod=O.causal_mod()),
+        "causal_alibi_window": O.gqa_attention_bwd(q, k, v, do, score_mod=O.compose_score_mods(
+            O.sliding_window_mod(Sl // 2 + 3), O.alibi_mod(Hq))),
+    }
+    mp.spawn(_bwd_worker, args=(world, _free_port(), q, k, v, do, want), nprocs=world, join=True)
 
 
 @pytest.mark.parametrize("world", [2, 4])
