@@ -68,6 +68,14 @@ class PagedParams(C.Structure):
     ]
 
 
+class RopeParams(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int), ("batch", i32), ("heads", i32), ("seq", i32), ("head_dim", i32),
+        ("x_strides", i64 * 3), ("out_strides", i64 * 3),
+        ("x", vp), ("out", vp), ("cos", vp), ("sin", vp), ("table_len", i32), ("positions", vp),
+    ]
+
+
 # Every symbol the header declares, with its ctypes signature.
 SIGNATURES = {
     "attn_fwd_workspace_size": (szt, [C.POINTER(FwdParams)]),
@@ -80,6 +88,7 @@ SIGNATURES = {
     "attn_paged_gather": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, vp, i32, vp, vp, vp]),
     "attn_paged_append": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, vp, i32, i32, vp, vp, vp, vp]),
     "attn_lse_merge": (C.c_int, [C.c_int, i64, i32, vp, vp, vp, vp, vp, vp]),
+    "attn_rope": (C.c_int, [C.POINTER(RopeParams), vp]),
     "attn_device_status": (C.c_int, [C.POINTER(i32)]),
     "attn_status_string": (C.c_char_p, [C.c_int]),
     "attn_version": (C.c_int, []),

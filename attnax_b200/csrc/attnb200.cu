@@ -837,6 +837,7 @@ int attn_paged_decode(const attn_paged_params_t* p, void* stream) {
 }  // extern "C"
 
 #include "paged_static.cu"
+#include "rope.cu"
 
 extern "C" int attn_lse_merge(attn_dtype_t dtype, int64_t rows, int32_t head_dim, float* o_acc,
                               float* lse_acc, const void* o_part, const float* lse_part, void* out,

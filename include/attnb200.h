@@ -24,6 +24,10 @@
  *                       (attnax/kernels/attention.py:662-671); the K/V
  *                       rotation (:673-674) is NCCL send/recv on the caller's
  *                       process group
+ *   attn_rope           apply_rope with cos/sin gathered by position ids
+ *                       (attnax/embeddings.py:126-184), the rotation
+ *                       MultiHeadAttention applies to Q and K before attention
+ *                       (attnax/attention.py:340-381)
  */
 #ifndef ATTNB200_H_
 #define ATTNB200_H_
@@ -164,6 +168,29 @@ int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool,
  * the merged rows are also written there in `dtype` (the final step). */
 int attn_lse_merge(attn_dtype_t dtype, int64_t rows, int32_t head_dim, float* o_acc, float* lse_acc,
                    const void* o_part, const float* lse_part, void* out, void* stream);
+
+/* ---- rotary position embedding ------------------------------------------- */
+/* Split-half RoPE on x (batch, heads, seq, head_dim), head_dim even and unit
+ * stride:  out[..., i] = x1 cos - x2 sin,  out[..., i + half] = x1 sin + x2 cos
+ * with x1 = x[..., i], x2 = x[..., i + half] and cos/sin the row of the
+ * [table_len][head_dim/2] tables (in `dtype`, as the reference builds them)
+ * at positions[b][s] (NULL: position s).  Positions wrap once when negative
+ * and clamp to the table, like the reference's array indexing.  Math in fp32;
+ * out may alias x. */
+typedef struct {
+  attn_dtype_t dtype;        /* x, out, cos, sin */
+  int32_t batch, heads, seq, head_dim;
+  int64_t x_strides[3];      /* elements: batch, head, seq */
+  int64_t out_strides[3];
+  const void* x;
+  void* out;
+  const void* cos;
+  const void* sin;
+  int32_t table_len;
+  const int32_t* positions;  /* [batch][seq] or NULL */
+} attn_rope_params_t;
+
+int attn_rope(const attn_rope_params_t* p, void* stream);
 
 /* ---- diagnostics -------------------------------------------------------- */
 /* Reads and clears the device status word that bounded waits set on

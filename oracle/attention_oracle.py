@@ -29,7 +29,8 @@ __all__ = [
     "ring_attention_partitioned", "PagedKVCache", "init_paged_kv_cache",
     "allocate_blocks", "append_kv", "gather_kv", "paged_attention",
     "paged_attention_batched", "softmax_scale", "bf16_round", "KVLayerCache",
-    "init_kv_layer_cache", "update_kv_layer_cache", "kv_cache_attention",
+    "init_kv_layer_cache", "update_kv_layer_cache", "kv_cache_attention", "rope_inv_freq",
+    "rope_cos_sin_table", "rope_cos_sin_from_positions", "apply_rope",
 ]
 
 
@@ -639,3 +640,34 @@ def kv_cache_attention(query, cache, *, mask=None, score_mod=None):
     concatenated history (attnax/attention.py:386-400, :32-39)."""
     n = int(cache.length)
     return gqa_attention(query, cache.keys[:, :, :n], cache.values[:, :, :n], mask=mask, score_mod=score_mod)
+
+
+# ----------------------------------------------------------------------------
+# embeddings.py: rotary position embedding (RoPE)
+# ----------------------------------------------------------------------------
+
+def rope_inv_freq(head_dim, base, dtype=np.float32):
+    """``base ** (-2i / head_dim)`` computed in ``dtype`` (embeddings.py:86-100)."""
+    half = head_dim // 2
+    return (1.0 / (base ** (np.arange(0, half, dtype=dtype) / half))).astype(dtype)
+
+
+def rope_cos_sin_table(max_seq_len, head_dim, base, dtype=np.float32):
+    """cos/sin of ``position * inv_freq`` with positions and products in
+    ``dtype`` (embeddings.py:103-123): ``(max_seq_len, head_dim // 2)`` each."""
+    inv = rope_inv_freq(head_dim, base, dtype)
+    freqs = np.outer(np.arange(max_seq_len, dtype=dtype), inv).astype(dtype)
+    return np.cos(freqs).astype(dtype), np.sin(freqs).astype(dtype)
+
+
+def rope_cos_sin_from_positions(position_ids, head_dim, base, table_len, dtype=np.float32):
+    """Table rows gathered by ``position_ids (B, S)`` (embeddings.py:162-184)."""
+    cos_t, sin_t = rope_cos_sin_table(table_len, head_dim, base, dtype)
+    return cos_t[position_ids], sin_t[position_ids]
+
+
+def apply_rope(x, cos, sin):
+    """Split-half rotation ``(x1 cos - x2 sin, x1 sin + x2 cos)`` (embeddings.py:126-159)."""
+    half = x.shape[-1] // 2
+    x1, x2 = x[..., :half], x[..., half:]
+    return np.concatenate([x1 * cos - x2 * sin, x1 * sin + x2 * cos], axis=-1)

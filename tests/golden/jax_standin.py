@@ -82,7 +82,7 @@ def _make_jnp():
     m.dtype = np.dtype
     m.finfo = np.finfo
     for name in ("where", "transpose", "sum", "exp", "broadcast_to", "maximum", "max",
-                 "abs", "tril", "repeat", "concatenate", "minimum"):
+                 "abs", "tril", "repeat", "concatenate", "minimum", "outer", "cos", "sin"):
         setattr(m, name, _wrap_fn(getattr(np, name)))
     m.einsum = lambda spec, *ops: _w(np.einsum(spec, *ops, optimize=True))
     m.dot = lambda a, b: _w(np.dot(a, b))

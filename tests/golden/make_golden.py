@@ -5,7 +5,8 @@ Run from the repository root where the attnax reference checkout is present:
     python tests/golden/make_golden.py [--ref /root/reference]
 
 The reference's hot-path modules (``attnax/kernels/*.py``,
-``attnax/paged_cache.py``, ``attnax/masking.py``) are imported unmodified on
+``attnax/paged_cache.py``, ``attnax/masking.py``, ``attnax/cache.py``,
+``attnax/embeddings.py``) are imported unmodified on
 top of ``jax_standin`` (numpy in place of ``jax.numpy``) and evaluated on
 seeded ``numpy.random.default_rng`` inputs.  Inputs and outputs are stored
 in ``golden_*.npz``; the tests read only those files.
@@ -34,6 +35,25 @@ def load_reference(ref_root: pathlib.Path):
     import attnax.masking as M  # noqa: E402
     import attnax.paged_cache as PC  # noqa: E402
     return K, M, PC
+
+
+def make_rope(ref_root: pathlib.Path):
+    """RoPE (``attnax/embeddings.py``): cos/sin tables built in the output dtype
+    (float32 and float16), gathered by position ids, applied split-half."""
+    import attnax.embeddings as E  # noqa: E402
+    out = {}
+    rng = np.random.default_rng(7)
+    B, H, S, D, table, base = 2, 3, 24, 16, 3000, 10000.0
+    pos = rng.integers(0, table, size=(B, S)).astype(np.int32)
+    out["rope_pos"] = pos
+    for name, dt in (("f32", np.float32), ("f16", np.float16)):
+        cos_t, sin_t = E.rope_cos_sin_table(table, D, base, dt)
+        cos, sin = E.rope_cos_sin_from_positions(A(pos), D, base, table, dt)
+        x = rnd(rng, (B, H, S, D)).astype(dt)
+        y = E.apply_rope(A(x), A(np.asarray(cos))[:, None], A(np.asarray(sin))[:, None])
+        out.update({f"rope_cos_{name}": np.asarray(cos_t), f"rope_sin_{name}": np.asarray(sin_t),
+                    f"rope_x_{name}": x, f"rope_y_{name}": np.asarray(y)})
+    np.savez_compressed(HERE / "golden_rope.npz", **out)
 
 
 def make_kvcache(ref_root: pathlib.Path, K):
@@ -86,13 +106,17 @@ def A(x):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=["kvcache"], default=None,
+    ap.add_argument("--only", choices=["kvcache", "rope"], default=None,
                     help="write only this fixture (leaves the other files untouched)")
     args = ap.parse_args()
     K, M, PC = load_reference(pathlib.Path(args.ref))
     if args.only == "kvcache":
         make_kvcache(pathlib.Path(args.ref), K)
         print("golden_kvcache.npz written to", HERE)
+        return
+    if args.only == "rope":
+        make_rope(pathlib.Path(args.ref))
+        print("golden_rope.npz written to", HERE)
         return
     out = {}
 
@@ -247,6 +271,7 @@ def main():
     out["ring_unbound"] = np.asarray(K.ring_attention(A(q), A(k), A(v), axis_name="not_bound"))
     np.savez_compressed(HERE / "golden_ring.npz", **out)
     make_kvcache(pathlib.Path(args.ref), K)
+    make_rope(pathlib.Path(args.ref))
     print("golden vectors written to", HERE)
 
 

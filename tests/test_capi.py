@@ -49,7 +49,8 @@ def test_ctypes_layout_matches_c_compiler(tmp_path):
     if shutil.which("gcc") is None:
         pytest.skip("gcc not available")
     structs = {"attn_mask_t": _lib.AttnMask, "attn_fwd_params_t": _lib.FwdParams,
-               "attn_bwd_params_t": _lib.BwdParams, "attn_paged_params_t": _lib.PagedParams}
+               "attn_bwd_params_t": _lib.BwdParams, "attn_paged_params_t": _lib.PagedParams,
+               "attn_rope_params_t": _lib.RopeParams}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{ROOT}/include/attnb200.h"',
              "int main(void) {"]
     for cname, py in structs.items():

@@ -198,6 +198,28 @@ def test_kv_layer_cache_update_host_logic_golden():
                                          dtype=torch.float32, device="cpu")) == 3
 
 
+def test_rope_golden():
+    """RoPE (embeddings.py): tables in the output dtype, gather by position,
+    split-half rotation -- the oracle bit for bit, and the library's torch table
+    construction (here on host tensors) within one ulp of the table dtype."""
+    import torch
+
+    import attnax_b200 as ax
+
+    d = load("rope")
+    pos = d["rope_pos"]
+    for name, dt, tdt, tol in (("f32", np.float32, torch.float32, 1e-6), ("f16", np.float16, torch.float16, 1e-3)):
+        c, s = O.rope_cos_sin_table(3000, 16, 10000.0, dt)
+        np.testing.assert_array_equal(c, d[f"rope_cos_{name}"])
+        np.testing.assert_array_equal(s, d[f"rope_sin_{name}"])
+        cp, sp = O.rope_cos_sin_from_positions(pos, 16, 10000.0, 3000, dt)
+        np.testing.assert_array_equal(O.apply_rope(d[f"rope_x_{name}"], cp[:, None], sp[:, None]),
+                                      d[f"rope_y_{name}"])
+        tc, ts = ax.rope_cos_sin_table(3000, 16, 10000.0, tdt, device="cpu")
+        np.testing.assert_allclose(tc.float().numpy(), d[f"rope_cos_{name}"].astype(np.float32), atol=tol)
+        np.testing.assert_allclose(ts.float().numpy(), d[f"rope_sin_{name}"].astype(np.float32), atol=tol)
+
+
 def test_ring_unbound_axis_falls_back_golden():
     d = load("ring")
     out = O.standard_attention(d["ring_q"], d["ring_k"], d["ring_v"])
