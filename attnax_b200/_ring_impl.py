@@ -82,18 +82,19 @@ def redeal(sched: RingSchedule, ops, tensors, to_work: bool):
     """Moves chunk buffers between the public layout and the ring layout.
 
     ``tensors`` is a list of tensors (B, H, rows, D) in the source layout;
-    returns the same tensors in the destination layout.
+    returns the same tensors in the destination layout.  All tensors travel
+    in one batched exchange (messages between two ranks pair up in tensor
+    order on both sides).
     """
     P, r = sched.P, sched.r
     src_chunks = sched.public(r) if to_work else sched.held(r)
     dst_chunks = sched.held(r) if to_work else sched.public(r)
     dst_of = sched.worker_of if to_work else (lambda c: sched.chunk(c).owner)
     src_of = (lambda c: sched.chunk(c).owner) if to_work else sched.worker_of
-    outs = []
+    sends, recvs, all_dst = [], [], []
     for t in tensors:
         parts_src = list(torch.split(t, sched.C, dim=2))
         parts_dst = [None] * len(dst_chunks)
-        sends, recvs = [], []
         for i, c in enumerate(src_chunks):
             peer = dst_of(c)
             if peer == r:
@@ -105,9 +106,17 @@ def redeal(sched: RingSchedule, ops, tensors, to_work: bool):
                 buf = torch.empty_like(parts_src[0], memory_format=torch.contiguous_format)
                 parts_dst[j] = buf
                 recvs.append((buf, src_of(c)))
-        ops.exchange(sends, recvs)
-        outs.append(torch.cat(parts_dst, dim=2) if len(parts_dst) > 1 else parts_dst[0].contiguous())
-    return outs
+        all_dst.append(parts_dst)
+    ops.exchange(sends, recvs)
+    return [torch.cat(p, dim=2) if len(p) > 1 else p[0].contiguous() for p in all_dst]
+
+
+def _pair_full(band, q_start, kv_start, n):
+    """True when the band keeps every (q, kv) pair of two n-row chunks."""
+    if band is None:
+        return True
+    lo, hi = band
+    return q_start - (kv_start + n - 1) >= lo and (q_start + n - 1) - kv_start <= hi
 
 
 def ring_schedule_forward(q, k, v, *, ops, sched: RingSchedule, band, state=None):
@@ -133,12 +142,27 @@ def ring_schedule_forward(q, k, v, *, ops, sched: RingSchedule, band, state=None
         kv_chunks = [sched.chunk(c) for c in sched.held(owner)]
         k_parts = torch.split(kv[0], C, dim=2)
         v_parts = torch.split(kv[1], C, dim=2)
-        for qi, qc in enumerate(my_chunks):
-            for ki, kc in enumerate(kv_chunks):
-                if _pairs_all_masked(band, qc.start, kc.start, C):
-                    continue
-                o_p, lse_p = ops.attend(q_parts[qi], k_parts[ki], v_parts[ki], qc, kc)
-                ops.merge(acc[qi], o_p, lse_p)
+        pairs = [(qi, ki) for qi, qc in enumerate(my_chunks) for ki, kc in enumerate(kv_chunks)
+                 if not _pairs_all_masked(band, qc.start, kc.start, C)]
+        if getattr(ops, "position_free", False) and len(my_chunks) == 2 and len(pairs) == 2 and all(
+                _pair_full(band, my_chunks[qi].start, kv_chunks[ki].start, C) for qi, ki in pairs):
+            # Two fully kept pairs that share a kv chunk (or a q chunk) and whose
+            # scores do not depend on positions: one kernel over both q chunks
+            # (or both kv chunks) of the ring buffers.
+            (qa, ka), (qb, kb) = pairs
+            if ka == kb and qa != qb:
+                o_p, lse_p = ops.attend_full(q, k_parts[ka], v_parts[ka])
+                for qi in (0, 1):
+                    ops.merge(acc[qi], o_p[:, :, qi * C:(qi + 1) * C].contiguous(),
+                              lse_p[:, :, qi * C:(qi + 1) * C].contiguous())
+                pairs = []
+            elif qa == qb and ka != kb:
+                o_p, lse_p = ops.attend_full(q_parts[qa], kv[0], kv[1])
+                ops.merge(acc[qa], o_p, lse_p)
+                pairs = []
+        for qi, ki in pairs:
+            o_p, lse_p = ops.attend(q_parts[qi], k_parts[ki], v_parts[ki], my_chunks[qi], kv_chunks[ki])
+            ops.merge(acc[qi], o_p, lse_p)
         if nxt is not None:
             kv = ops.finish_rotate(nxt)
     outs = [ops.finalize(a, q_parts[0].dtype) for a in acc]
@@ -253,6 +277,13 @@ class KernelOps(DistExchange):
         super().__init__(group)
         self.score_mod, self.mask = score_mod, mask
         self.batch, self.heads_q, self.S, self.device = batch, heads_q, seq_local, device
+        from ._spec import flatten_mods
+        from .score_mods import CausalMod, SlidingWindowMod
+
+        # Only band selections (causal / sliding window): a fully kept pair's
+        # scores do not depend on positions.
+        self.position_free = mask is None and all(isinstance(p, (CausalMod, SlidingWindowMod))
+                                                  for p in flatten_mods(score_mod))
 
     def new_acc(self, q_part):
         B, H, n, D = q_part.shape
@@ -292,6 +323,16 @@ class KernelOps(DistExchange):
         from .flash import fwd_raw
 
         return fwd_raw(q.contiguous(), k.contiguous(), v.contiguous(), self._spec(q, k, qc, kc))
+
+    def attend_full(self, q, k, v):
+        """Unmasked attention of any q rows on any kv rows (pairs the band keeps whole)."""
+        from ._spec import build_spec
+        from .flash import fwd_raw
+
+        spec = build_spec(None, None, batch=self.batch, heads_q=self.heads_q, seq_q=q.shape[2],
+                          seq_kv=k.shape[2], device=self.device)
+        spec.fix_masked_rows = False
+        return fwd_raw(q.contiguous(), k.contiguous(), v.contiguous(), spec)
 
     def grad(self, q, k, v, o, lse, do, qc, kc):
         """Partial (dq, dk, dv) of one chunk pair from the global lse (rows with no

@@ -33,6 +33,10 @@ class OracleOps:
 
         self.x = DistExchange(group)
         self.mod, self.mask, self.rep = mod, mask, hq // hkv
+        # True when the chain only selects a band (none / causal / window), as
+        # KernelOps decides from the tagged mods: the schedule may then batch
+        # fully kept pairs into position-free calls
+        self.position_free = False
 
     def exchange(self, sends, recvs):
         self.x.exchange(sends, recvs)
@@ -60,6 +64,12 @@ class OracleOps:
                                           q_offset=qc.start, kv_offset=kc.start)
         o[empty] = 0.0
         lse[empty] = -np.inf
+        return torch.from_numpy(o), torch.from_numpy(lse)
+
+    def attend_full(self, q, k, v):
+        qn, kn, vn = (t.double().numpy() for t in (q, k, v))
+        kn, vn = np.repeat(kn, self.rep, 1), np.repeat(vn, self.rep, 1)
+        o, lse = O.standard_attention_lse(qn, kn, vn)
         return torch.from_numpy(o), torch.from_numpy(lse)
 
     def grad(self, q, k, v, o, lse, do, qc, kc):
@@ -128,6 +138,7 @@ def _worker(rank, world, port, q, k, v, want):
                 mask = local_mask
             sched = RingSchedule(world, rank, S, zig)
             ops = OracleOps(None, mod, mask, q.shape[1], k.shape[1])
+            ops.position_free = case in ("none", "causal")
             tq, tk, tv = (torch.from_numpy(np.ascontiguousarray(x[:, :, sl])).double() for x in (q, k, v))
             out, _ = ring_schedule_forward(tq, tk, tv, ops=ops, sched=sched, band=band)
             np.testing.assert_allclose(out.numpy(), want[case][:, :, sl], atol=1e-10, rtol=1e-10,
@@ -155,6 +166,7 @@ def _bwd_worker(rank, world, port, q, k, v, do, want):
                 band, zig = (0, S // 2 + 2), True
             sched = RingSchedule(world, rank, S, zig)
             ops = OracleOps(None, mod, None, q.shape[1], k.shape[1])
+            ops.position_free = case in ("none", "causal")
             tq, tk, tv, tdo = (torch.from_numpy(np.ascontiguousarray(x[:, :, sl])).double() for x in (q, k, v, do))
             st = {}
             ring_schedule_forward(tq, tk, tv, ops=ops, sched=sched, band=band, state=st)
