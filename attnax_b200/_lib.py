@@ -16,6 +16,10 @@ LIB_PATH = os.path.join(_HERE, "libattnb200.so")
 ATTN_OK, ATTN_ERR_INVALID, ATTN_ERR_UNSUPPORTED, ATTN_ERR_CUDA, ATTN_ERR_NCCL, \
     ATTN_ERR_WORKSPACE, ATTN_ERR_TIMEOUT = range(7)
 ATTN_F32, ATTN_BF16, ATTN_F16 = 0, 1, 2
+# Device status codes (attn_device_status): bounded-wait timeouts and notices.
+STATUS_TIMEOUTS = (0x101, 0x102, 0x103, 0x104)
+NOTICE_CONTEXT_OVERRUN = 0x201   # a paged decode met a length above max_context
+NOTICE_TABLE_OVERRUN = 0x202     # a paged decode met a length past its block-table row
 
 i32, i64, f32, vp, szt = C.c_int32, C.c_int64, C.c_float, C.c_void_p, C.c_size_t
 
@@ -85,8 +89,9 @@ SIGNATURES = {
     "attn_paged_decode_workspace_size": (szt, [C.POINTER(PagedParams)]),
     "attn_paged_decode": (C.c_int, [C.POINTER(PagedParams), vp]),
     "attn_paged_decode_static": (C.c_int, [C.POINTER(PagedParams), vp]),
-    "attn_paged_gather": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, vp, i32, vp, vp, vp]),
-    "attn_paged_append": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, vp, i32, i32, vp, vp, vp, vp]),
+    "attn_paged_gather": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, i32, vp, i32, i32, vp, vp, vp]),
+    "attn_paged_append": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp, vp]),
+    "attn_paged_physical_page": (i64, [i32, i32]),
     "attn_lse_merge": (C.c_int, [C.c_int, i64, i32, vp, vp, vp, vp, vp, vp]),
     "attn_rope": (C.c_int, [C.POINTER(RopeParams), vp]),
     "attn_device_status": (C.c_int, [C.POINTER(i32)]),

@@ -31,6 +31,15 @@ enum TileState : int { kSkip = 0, kPartial = 1, kFull = 2 };
 constexpr int kDocTile = 128;
 
 __host__ __device__ inline long long ll_min(long long a, long long b) { return a < b ? a : b; }
+
+// Pool page that block-table entry `e` selects in a pool of `num_blocks`
+// pages, read as JAX's array indexing reads pool[block_ids]
+// (attnax/paged_cache.py:222-230): a negative entry counts from the end of
+// the pool, then the index is clamped into [0, num_blocks).
+__host__ __device__ inline long long paged_phys_page(long long e, int num_blocks) {
+  if (e < 0) e += num_blocks;
+  return e < 0 ? 0 : (e >= num_blocks ? (long long)num_blocks - 1 : e);
+}
 __host__ __device__ inline long long ll_max(long long a, long long b) { return a > b ? a : b; }
 
 // Classifies the tile [q0,q1) x [k0,k1) of batch b (local positions).

@@ -330,13 +330,19 @@ const char* attn_status_string(int s) {
 }
 
 int attn_device_status(int32_t* status) {
-  int v = 0;
+  int v = 0, n = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return ATTN_ERR_CUDA;
   if (cudaMemcpyFromSymbol(&v, g_status, sizeof(int)) != cudaSuccess) return ATTN_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&n, g_notice, sizeof(int)) != cudaSuccess) return ATTN_ERR_CUDA;
   const int zero = 0;
   if (cudaMemcpyToSymbol(g_status, &zero, sizeof(int)) != cudaSuccess) return ATTN_ERR_CUDA;
-  if (status) *status = v;
+  if (cudaMemcpyToSymbol(g_notice, &zero, sizeof(int)) != cudaSuccess) return ATTN_ERR_CUDA;
+  if (status) *status = v ? v : n;
   return ATTN_OK;
+}
+
+int64_t attn_paged_physical_page(int32_t entry, int32_t num_blocks) {
+  return num_blocks > 0 ? paged_phys_page(entry, num_blocks) : -1;
 }
 
 size_t attn_fwd_workspace_size(const attn_fwd_params_t* p) {
@@ -649,13 +655,15 @@ static int paged_vec_bytes(int row_bytes) {
 extern "C" {
 
 int attn_paged_gather(attn_dtype_t dtype, const void* key_pool, const void* value_pool,
-                      int32_t block_size, int32_t heads_kv, int32_t head_dim,
-                      const int32_t* block_table_row, int32_t seq_len, void* keys_out,
+                      int32_t num_blocks, int32_t block_size, int32_t heads_kv, int32_t head_dim,
+                      const int32_t* block_table_row, int32_t max_blocks, int32_t seq_len, void* keys_out,
                       void* values_out, void* stream) {
-  if (!key_pool || !value_pool || !block_table_row || block_size <= 0 || heads_kv <= 0 ||
-      head_dim <= 0 || seq_len < 0)
+  if (!key_pool || !value_pool || !block_table_row || num_blocks <= 0 || block_size <= 0 || heads_kv <= 0 ||
+      head_dim <= 0 || max_blocks <= 0 || seq_len < 0)
     return ATTN_ERR_INVALID;
   if (seq_len == 0) return ATTN_OK;
+  // gather_kv cannot reshape fewer table entries than the length needs.
+  if ((long long)seq_len > (long long)max_blocks * block_size) return ATTN_ERR_INVALID;
   if (!keys_out || !values_out) return ATTN_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int row_bytes = heads_kv * head_dim * (int)dtype_size(dtype);
@@ -664,15 +672,12 @@ int attn_paged_gather(attn_dtype_t dtype, const void* key_pool, const void* valu
                        reinterpret_cast<uintptr_t>(keys_out) | reinterpret_cast<uintptr_t>(values_out);
   while (vb > 2 && al % vb) vb /= 2;
   const int row_vecs = row_bytes / vb;
-  // num_blocks is only needed to wrap negative ids; callers pass tables of
-  // valid ids, so a negative entry wraps from the end as numpy would.  The
-  // pool size is not part of this signature: wrap against INT_MAX-safe 0.
   const long long n = (long long)seq_len * row_vecs;
   const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
 #define ATTN_GATHER(V)                                                                          \
   paged::gather_kernel<V><<<grid, 256, 0, st>>>(                                               \
       reinterpret_cast<const V*>(key_pool), reinterpret_cast<const V*>(value_pool), block_size, \
-      row_vecs, block_table_row, seq_len, 0, reinterpret_cast<V*>(keys_out),                    \
+      row_vecs, block_table_row, seq_len, num_blocks, reinterpret_cast<V*>(keys_out),           \
       reinterpret_cast<V*>(values_out))
   if (vb == 16) ATTN_GATHER(uint4);
   else if (vb == 8) ATTN_GATHER(uint2);
@@ -682,12 +687,12 @@ int attn_paged_gather(attn_dtype_t dtype, const void* key_pool, const void* valu
   return launch_status();
 }
 
-int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool, int32_t block_size,
-                      int32_t heads_kv, int32_t head_dim, const int32_t* block_table_row,
-                      int32_t start, int32_t chunk, const void* keys_new, const void* values_new,
-                      int32_t* bad_slot, void* stream) {
-  if (!key_pool || !value_pool || !block_table_row || block_size <= 0 || heads_kv <= 0 ||
-      head_dim <= 0 || start < 0 || chunk < 0)
+int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool, int32_t num_blocks,
+                      int32_t block_size, int32_t heads_kv, int32_t head_dim, const int32_t* block_table_row,
+                      int32_t max_blocks, int32_t start, int32_t chunk, const void* keys_new,
+                      const void* values_new, int32_t* bad_slot, void* stream) {
+  if (!key_pool || !value_pool || !block_table_row || num_blocks <= 0 || block_size <= 0 || heads_kv <= 0 ||
+      head_dim <= 0 || max_blocks <= 0 || start < 0 || chunk < 0)
     return ATTN_ERR_INVALID;
   if (chunk == 0) return ATTN_OK;
   if (!keys_new || !values_new) return ATTN_ERR_INVALID;
@@ -696,8 +701,8 @@ int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool, int3
     // Check pass only: the caller reads bad_slot (pre-set to INT_MAX) and
     // calls again with bad_slot == NULL to write, so a failed append writes
     // nothing (append_kv raises before any update, paged_cache.py:180-188).
-    paged::append_check_kernel<<<(chunk + 255) / 256, 256, 0, st>>>(block_table_row, block_size, start,
-                                                                      chunk, bad_slot);
+    paged::append_check_kernel<<<(chunk + 255) / 256, 256, 0, st>>>(block_table_row, max_blocks, block_size,
+                                                                      start, chunk, bad_slot);
     return launch_status();
   }
   const int row_bytes = heads_kv * head_dim * (int)dtype_size(dtype);
@@ -708,10 +713,10 @@ int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool, int3
   const int row_vecs = row_bytes / vb;
   const long long n = (long long)chunk * row_vecs;
   const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
-#define ATTN_APPEND(V)                                                                        \
-  paged::append_kernel<V><<<grid, 256, 0, st>>>(                                             \
-      reinterpret_cast<V*>(key_pool), reinterpret_cast<V*>(value_pool), block_size, row_vecs, \
-      block_table_row, start, chunk, reinterpret_cast<const V*>(keys_new),                    \
+#define ATTN_APPEND(V)                                                                          \
+  paged::append_kernel<V><<<grid, 256, 0, st>>>(                                               \
+      reinterpret_cast<V*>(key_pool), reinterpret_cast<V*>(value_pool), block_size, row_vecs,   \
+      block_table_row, num_blocks, max_blocks, start, chunk, reinterpret_cast<const V*>(keys_new), \
       reinterpret_cast<const V*>(values_new))
   if (vb == 16) ATTN_APPEND(uint4);
   else if (vb == 8) ATTN_APPEND(uint2);

@@ -3,8 +3,9 @@
 // Pool layout (the reference's): [num_blocks, block_size, heads_kv, head_dim],
 // token-major with heads interleaved.  Logical token t of sequence s lives in
 // physical page block_table[s, t / block_size], row t % block_size
-// (paged_cache.py:222-230).  Negative table entries index from the end of
-// the pool, as numpy/JAX fancy indexing does.
+// (paged_cache.py:222-230).  Table entries are read the way JAX's array
+// indexing reads them there: a negative entry counts from the end of the
+// pool, and the result is clamped into the pool (paged_phys_page).
 //
 // Decode is split-K: CTA = (split, kv head, sequence, row group).  A TMA
 // warp streams each page's K and V slice ([block_size, head_dim] at a
@@ -23,8 +24,16 @@ namespace attnb200 {
 namespace paged {
 
 __device__ __forceinline__ long long phys_page(const int32_t* table_row, int i, int num_blocks) {
-  long long p = table_row[i];
-  return p < 0 ? p + num_blocks : p;
+  return paged_phys_page(table_row[i], num_blocks);
+}
+
+// Logical page `lp` of a sequence bounded by its table row (max_blocks
+// entries).  A length beyond max_blocks * block_size (which the reference's
+// gather_kv cannot reshape) reads the row's last entry and leaves a notice.
+__device__ __forceinline__ int table_col(int lp, int max_blocks) {
+  if (lp < max_blocks) return lp;
+  atomicCAS(&g_notice, 0, kNoticeTableOverrun);
+  return max_blocks - 1;
 }
 
 // ------------------------------------------------------------ gather_kv ----
@@ -42,23 +51,30 @@ __global__ void gather_kernel(const V* kp, const V* vp, int bs, int row_vecs,
 }
 
 // ------------------------------------------------------------ append_kv ----
-__global__ void append_check_kernel(const int32_t* table_row, int bs, int start, int chunk,
+// Lowest logical page of the chunk that has no table slot (column past the
+// row) or an unallocated one (-1): append_kv raises for both before writing.
+__global__ void append_check_kernel(const int32_t* table_row, int max_blocks, int bs, int start, int chunk,
                                     int32_t* bad_slot) {
   for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < chunk; t += gridDim.x * blockDim.x) {
     const int logical = (start + t) / bs;
-    if (table_row[logical] < 0) atomicMin(bad_slot, logical);
+    if (logical >= max_blocks || table_row[logical] < 0) atomicMin(bad_slot, logical);
   }
 }
 
+// Per-token scatter.  A physical page at or past the end of the pool drops
+// its rows, as JAX's .at[].set drops out-of-bounds updates.
 template <typename V>
-__global__ void append_kernel(V* kp, V* vp, int bs, int row_vecs, const int32_t* table_row,
-                              int start, int chunk, const V* kn, const V* vn) {
+__global__ void append_kernel(V* kp, V* vp, int bs, int row_vecs, const int32_t* table_row, int num_blocks,
+                              int max_blocks, int start, int chunk, const V* kn, const V* vn) {
   const long long n = (long long)chunk * row_vecs;
   for (long long x = blockIdx.x * (long long)blockDim.x + threadIdx.x; x < n;
        x += (long long)gridDim.x * blockDim.x) {
     const int t = (int)(x / row_vecs), e = (int)(x % row_vecs);
     const int pos = start + t;
-    const long long dst = ((long long)table_row[pos / bs] * bs + pos % bs) * row_vecs + e;
+    if (pos / bs >= max_blocks) continue;
+    const long long page = table_row[pos / bs];
+    if (page < 0 || page >= num_blocks) continue;
+    const long long dst = (page * bs + pos % bs) * row_vecs + e;
     kp[dst] = kn[x];
     vp[dst] = vn[x];
   }
@@ -141,7 +157,7 @@ __global__ void __launch_bounds__(kThreads)
       for (int i = 0; i < npages; ++i) {
         const int s = i % S;
         if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, kStatusTimeoutLoad)) break;
-        const int pid = (int)phys_page(row, p0 + i, a.num_blocks);
+        const int pid = (int)phys_page(row, table_col(p0 + i, a.max_blocks), a.num_blocks);
         mbar_expect_tx(full(s), 4 * a.BS * 128);
         for (int c = 0; c < 2; ++c) {
           tma_load_3d(k_base + s * page_bytes + c * a.box_bytes, &tm_k, full(s), c * 64, hkv, pid * a.BS);
@@ -416,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 3)
         const int s = i % S;
         if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, kStatusTimeoutLoad)) break;
         const int tok = (u0 + i) * U;
-        const int pid = (int)phys_page(row, tok / a.BS, a.num_blocks);
+        const int pid = (int)phys_page(row, table_col(tok / a.BS, a.max_blocks), a.num_blocks);
         const int prow = pid * a.BS + tok % a.BS;  // pool row of the unit's first token
         mbar_expect_tx(full(s), 4 * U * 128);
         for (int c = 0; c < 2; ++c) {
@@ -599,8 +615,11 @@ __global__ void paged_combine_kernel(const float* part_o, const float* part_lse,
   const int ctx = seq_lens[seq];
   const long long prow = (long long)seq * Hq * Sq + row;
   T* orow = out + prow * D;
-  // max_context bounds the lengths by contract; clamp so a violation cannot read past the partials.
-  const int n = min((ctx + chunk_tokens - 1) / chunk_tokens, max_splits);
+  // max_context bounds the lengths by contract: a longer sequence is cut to
+  // the splits that exist (never read past the partials) and leaves a notice.
+  const int need = (ctx + chunk_tokens - 1) / chunk_tokens;
+  if (need > max_splits && threadIdx.x == 0) atomicCAS(&g_notice, 0, kNoticeContextOverrun);
+  const int n = min(need, max_splits);
   if (n == 0) {  // empty sequence: zeros (paged.py:53-54)
     for (int d = threadIdx.x; d < D; d += blockDim.x) orow[d] = from_f32<T>(0.f);
     return;

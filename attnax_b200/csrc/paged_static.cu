@@ -1,9 +1,10 @@
 // Allocation-free variant of the paged decode (attn_paged_decode_static).
 //
-// Some callers cannot allocate device memory: code that runs while a CUDA
-// graph is being captured, serving loops whose allocator forbids cudaMalloc
-// on the hot path (it synchronises the device), and embedders with a fixed
-// memory budget.  This entry point keeps the split-K partials in a
+// Some callers cannot allocate device memory for a workspace: serving loops
+// whose allocator forbids cudaMalloc on the decode path (it synchronises the
+// device and stalls every stream), embedders that run the library inside a
+// fixed device-memory budget, and plugin hosts that hand a kernel only its
+// inputs and outputs.  This entry point keeps the split-K partials in a
 // file-scope device array instead of a caller workspace.  It launches the
 // same decode and combine kernels as attn_paged_decode.
 #include <mutex>
@@ -17,16 +18,37 @@ static __device__ __align__(256) float g_scratch[kScratchFloats];
 
 constexpr int kMaxDevices = 64;
 static float* g_scratch_ptr[kMaxDevices];
+static CUcontext g_scratch_ctx[kMaxDevices];
 static std::mutex g_scratch_mu;
 
+// The calling thread's current CUDA context (null before the runtime made one).
+static CUcontext current_context() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  });
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
 // Device address of g_scratch for the current device.  In host code the
-// symbol is only a host-side stand-in, so the address is looked up once per
-// device, with that device current, and cached.
+// symbol is only a host-side stand-in, so the address is looked up with the
+// device current (cudaGetSymbolAddress) and cached per device together with
+// the context it was looked up in; a call under another context (after a
+// cudaDeviceReset, or from a non-primary context, where the module and its
+// array may sit elsewhere) looks it up again.
 static int scratch_address(float** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ATTN_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  const CUcontext ctx = current_context();
+  if (!g_scratch_ptr[dev] || !ctx || ctx != g_scratch_ctx[dev]) {
     void* ptr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
     if (e != cudaSuccess || !ptr) {
@@ -34,6 +56,7 @@ static int scratch_address(float** out) {
       return ATTN_ERR_CUDA;
     }
     g_scratch_ptr[dev] = static_cast<float*>(ptr);
+    g_scratch_ctx[dev] = current_context();  // the lookup made the device's context current
   }
   *out = g_scratch_ptr[dev];
   return ATTN_OK;

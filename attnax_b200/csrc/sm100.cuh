@@ -22,6 +22,16 @@ __device__ int g_status;
 enum : int { kStatusTimeoutLoad = 0x101, kStatusTimeoutMma = 0x102, kStatusTimeoutSoftmax = 0x103,
              kStatusTimeoutOther = 0x104 };
 
+// Set (first writer wins) when a kernel met input outside its contract that
+// it could still process safely (results follow the documented clamping).
+// Unlike g_status it does not stop other kernels' waits.
+__device__ int g_notice;
+
+enum : int {
+  kNoticeContextOverrun = 0x201,  // a seq_lengths entry above max_context: cut to the planned splits
+  kNoticeTableOverrun = 0x202     // a sequence longer than its block-table row: last entry reused
+};
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

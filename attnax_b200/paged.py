@@ -92,8 +92,8 @@ def append_kv(cache: PagedKVCache, sequence_idx: int, keys_new: torch.Tensor,
         raise ValueError("append_kv past max_blocks_per_seq")
     stream = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     args = (dtype_code(cache.key_pool.dtype), cache.key_pool.data_ptr(), cache.value_pool.data_ptr(),
-            cache.block_size, cache.num_kv_heads, cache.head_dim, row.data_ptr(), start, chunk,
-            kn.data_ptr(), vn.data_ptr())
+            cache.num_blocks, cache.block_size, cache.num_kv_heads, cache.head_dim, row.data_ptr(), row.numel(),
+            start, chunk, kn.data_ptr(), vn.data_ptr())
     bad = torch.full((1,), 2**31 - 1, dtype=torch.int32, device=dev)
     _lib.check(lib.attn_paged_append(*args, bad.data_ptr(), stream), "attn_paged_append")
     bad_slot = int(bad.item())
@@ -117,9 +117,9 @@ def gather_kv(cache: PagedKVCache, sequence_idx: int):
         row = cache.block_table[sequence_idx].contiguous()
         stream = C.c_void_p(torch.cuda.current_stream(k.device).cuda_stream)
         _lib.check(lib.attn_paged_gather(dtype_code(k.dtype), cache.key_pool.data_ptr(),
-                                         cache.value_pool.data_ptr(), cache.block_size,
-                                         cache.num_kv_heads, cache.head_dim, row.data_ptr(), seq_len,
-                                         k.data_ptr(), v.data_ptr(), stream), "attn_paged_gather")
+                                         cache.value_pool.data_ptr(), cache.num_blocks, cache.block_size,
+                                         cache.num_kv_heads, cache.head_dim, row.data_ptr(), row.numel(),
+                                         seq_len, k.data_ptr(), v.data_ptr(), stream), "attn_paged_gather")
     return k, v, seq_len
 
 
@@ -129,7 +129,10 @@ def paged_decode_raw(query, cache: PagedKVCache, *, block_table=None, seq_length
 
     ``query`` is ``(num_seqs, Hq, Sq, D)``; returns the same shape.  With
     ``max_context`` given (an upper bound of the lengths) no host sync
-    happens.
+    happens; the bound is then the caller's promise, and a length above it
+    (or past its block-table row) is processed by the documented clamping
+    and reported by ``_lib.device_status()`` (``NOTICE_CONTEXT_OVERRUN`` /
+    ``NOTICE_TABLE_OVERRUN``) instead of raising.
     """
     lib = _lib.load()
     bt = cache.block_table if block_table is None else block_table
@@ -145,7 +148,12 @@ def paged_decode_raw(query, cache: PagedKVCache, *, block_table=None, seq_length
     if not query.is_cuda:
         raise RuntimeError("attnax_b200 kernels need CUDA tensors; there is no CPU path")
     if max_context is None:
+        # (one host sync; the lengths are then known to fit their table rows,
+        # which gather_kv in the reference needs to reshape them)
         max_context = int(sl.max()) if sl.numel() else 0
+        if max_context > bt.shape[1] * cache.block_size:
+            raise ValueError(f"a sequence length ({max_context}) exceeds max_blocks_per_seq * block_size "
+                             f"({bt.shape[1]} * {cache.block_size})")
     q = query.to(cache.key_pool.dtype).contiguous()
     out = torch.empty_like(q) if out is None else out
     p = _lib.PagedParams()

@@ -91,6 +91,17 @@ def paged_setup(scale, seed=0):
     return dict(nseq=nseq, ctx=ctx.astype(np.int32), bs=bs, nb=nb, table=table, Hq=32, Hkv=8, D=128)
 
 
+def paged_tensors(c, dev):
+    """Pools (N(0,1), bf16) and one decode query per sequence for ``paged_setup``."""
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(7)
+    kp = torch.randn(c["nb"], c["bs"], c["Hkv"], c["D"], generator=g, device=dev).to(torch.bfloat16)
+    vp = torch.randn(c["nb"], c["bs"], c["Hkv"], c["D"], generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(c["nseq"], c["Hq"], 1, c["D"], generator=g, device=dev).to(torch.bfloat16)
+    return kp, vp, q
+
+
 # ------------------------------------------------------------------ timing --
 
 class Clocks:
@@ -245,13 +256,20 @@ def run_flash(args, torch, dist, rank, world, peaks):
     launches = launches * args.steps // (args.steps + args.warmup)
     value = world * (fwd_flops + bwd_flops) / (ms * 1e-3) / 1e12
 
-    # e2e: public API (autograd flash_attention), every step's inputs copied
-    # from pinned host memory and its scalar result read back to the host.
-    # Copies run on a side stream one step ahead of the compute stream
-    # (double-buffered device inputs), so PCIe overlaps the kernels.
+    # e2e: public API (autograd flash_attention); every step copies q, k, v
+    # and dO from pinned host memory and copies the output and dQ, dK, dV
+    # back to pinned host memory.  Uploads run one step ahead on a side
+    # stream and downloads on another, so PCIe overlaps the kernels.
+    def e2e_step(tq, tk, tv, tdo):
+        tq, tk, tv = (t.detach().requires_grad_() for t in (tq, tk, tv))
+        o = ax.flash_attention(tq, tk, tv, score_mod=mod)
+        o.backward(tdo)
+        return o.detach(), tq.grad, tk.grad, tv.grad
+
+    host_res = [torch.empty_like(t).pin_memory() for t in (hq, hq, hk, hv)]  # out, dq, dk, dv
     e2e_steps = max(2, min(args.steps, 8))
-    e2e_ms = e2e_pipelined(torch, dist, world, dev, (hq, hk, hv, hdo), mod, ax, e2e_steps, warmup=2)
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hdo))
+    e2e_ms = e2e_pipelined(torch, dist, world, dev, (hq, hk, hv, hdo), host_res, e2e_step, e2e_steps, warmup=2)
+    h2d, d2h = nbytes((hq, hk, hv, hdo)), nbytes(host_res)
     e2e_value = world * (fwd_flops + bwd_flops) / (e2e_ms * 1e-3) / 1e12
 
     peak_b, peak_s = peaks["bf16_tflops"], peaks["bf16_tflops_sustained"]
@@ -282,7 +300,8 @@ def run_flash(args, torch, dist, rank, world, peaks):
         "fwd_tflops": kern["fwd"]["tflops"], "bwd_tflops": kern["bwd"]["tflops"], "kernels": kern,
         "roofline": roof,
         "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 3)},
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+                "returned": "output, dQ, dK, dV to pinned host memory every step"},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
         "peaks_source": PEAKS_SRC,
@@ -300,22 +319,29 @@ TRAFFIC = {"fwd": 4 * 133.2e6, "bwd": 4 * (222.7e6 + 427.7e6 + 176.3e6)}
 PAGED_TRAFFIC_RATIO = (1.100622e9 + 6.36672e6) / 1.1001e9
 
 
-def e2e_pipelined(torch, dist, world, dev, host, mod, ax, steps, warmup):
-    """ms per step of the public-API fwd+bwd with H2D copies one step ahead."""
-    copy = torch.cuda.Stream()
+def e2e_pipelined(torch, dist, world, dev, host_in, host_out, compute, steps, warmup):
+    """ms per step of ``compute`` through the public API, end to end.
+
+    Every step's inputs are copied from the pinned ``host_in`` buffers (on an
+    upload stream, one step ahead, into two device buffer sets) and every
+    step's results -- the tuple ``compute`` returns -- are copied back into
+    the pinned ``host_out`` buffers (on a download stream).  The timed region
+    ends when the last step's results have reached the host.
+    """
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
     comp = torch.cuda.current_stream()
-    bufs = [[torch.empty_like(h, device=dev) for h in host] for _ in range(2)]
+    bufs = [[torch.empty_like(h, device=dev) for h in host_in] for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
     for e in free:
         e.record(comp)
 
     def upload(slot):
-        with torch.cuda.stream(copy):
-            copy.wait_event(free[slot])
-            for d, h in zip(bufs[slot], host):
+        with torch.cuda.stream(up):
+            up.wait_event(free[slot])
+            for d, h in zip(bufs[slot], host_in):
                 d.copy_(h, non_blocking=True)
-            copied[slot].record(copy)
+            copied[slot].record(up)
 
     def run(n):
         upload(0)
@@ -324,13 +350,16 @@ def e2e_pipelined(torch, dist, world, dev, host, mod, ax, steps, warmup):
             if i + 1 < n:
                 upload((i + 1) % 2)
             comp.wait_event(copied[slot])
-            tq, tk, tv, tdo = bufs[slot]
-            tq, tk, tv = (t.detach().requires_grad_() for t in (tq, tk, tv))
-            out = ax.flash_attention(tq, tk, tv, score_mod=mod)
-            out.backward(tdo)
-            loss = (out.detach().float() * tdo.float()).sum()
+            res = compute(*bufs[slot])
             free[slot].record(comp)
-            loss.to("cpu", non_blocking=False)
+            done = torch.cuda.Event()
+            done.record(comp)
+            with torch.cuda.stream(down):
+                down.wait_event(done)
+                for h, d in zip(host_out, res):
+                    h.copy_(d, non_blocking=True)
+                    d.record_stream(down)
+        comp.wait_stream(down)
 
     run(warmup)
     torch.cuda.synchronize()
@@ -349,6 +378,10 @@ def e2e_pipelined(torch, dist, world, dev, host, mod, ax, steps, warmup):
     return ms / steps
 
 
+def nbytes(ts):
+    return sum(t.numel() * t.element_size() for t in ts)
+
+
 def run_paged(args, torch, peaks):
     import attnax_b200 as ax
     from attnax_b200 import _lib
@@ -356,11 +389,8 @@ def run_paged(args, torch, peaks):
 
     c = paged_setup(args.scale)
     dev = torch.device("cuda", torch.cuda.current_device())
-    g = torch.Generator(device=dev).manual_seed(7)
-    kp = torch.randn(c["nb"], c["bs"], c["Hkv"], c["D"], generator=g, device=dev).to(torch.bfloat16)
-    vp = torch.randn(c["nb"], c["bs"], c["Hkv"], c["D"], generator=g, device=dev).to(torch.bfloat16)
+    kp, vp, q = paged_tensors(c, dev)
     cache = ax.PagedKVCache(kp, vp, torch.tensor(c["table"], device=dev), torch.tensor(c["ctx"], device=dev))
-    q = torch.randn(c["nseq"], c["Hq"], 1, c["D"], generator=g, device=dev).to(torch.bfloat16)
     out = torch.empty_like(q)
     maxc = int(c["ctx"].max())
     ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
@@ -448,50 +478,147 @@ def run_document(args, torch, peaks):
                          "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4)}}
 
 
-def run_ring(args, torch, dist, rank, world, peaks):
-    """Ring attention, B1 Hq32 Hkv8 D128 causal, global S split over the ranks (strong scaling)."""
-    import attnax_b200 as ax
-    from attnax_b200.ring import ring_forward
+RING = dict(S=131072, Hq=32, Hkv=8, D=128)
 
-    S = 131072 if args.scale == "full" else 16384
-    Hq, Hkv, D = 32, 8, 128
+
+def ring_shard(kind, rank, world, S, dtype=np.float32):
+    """Rank ``rank``'s contiguous shard of the ring workload's q, k or v:
+    N(0,1) drawn in fp32 from default_rng((seed, rank)), B1, (heads, S/P, D)."""
+    heads = RING["Hq"] if kind == "q" else RING["Hkv"]
+    seed = {"q": 31, "k": 32, "v": 33}[kind]
+    Sl = S // world
+    return np.random.default_rng((seed, rank)).standard_normal((1, heads, Sl, RING["D"]), dtype=dtype)
+
+
+def run_ring(args, torch, dist, rank, world, peaks, headline=False):
+    """Ring attention, B1 Hq32 Hkv8 D128 causal, global S split over the ranks (strong scaling).
+
+    One step = one ring forward over the whole sequence (every rank its S/P
+    shard).  At N>1 this is the headline line: it also carries the
+    end-to-end number through ``ring_attention`` (host shards in, host
+    output shard out), clocks, the launch count, and an in-run parity check
+    of sampled output rows of every shard against the oracle.
+    """
+    import attnax_b200 as ax
+    from attnax_b200 import _lib
+    from attnax_b200.ring import bind_axis, ring_forward
+
+    S = RING["S"] if args.scale == "full" else 16384
+    Hq, Hkv, D = RING["Hq"], RING["Hkv"], RING["D"]
     Sl = S // world
     dev = torch.device("cuda", torch.cuda.current_device())
-    g = torch.Generator(device=dev).manual_seed(11 + rank)
-    q = torch.randn(1, Hq, Sl, D, generator=g, device=dev).to(torch.bfloat16)
-    k = torch.randn(1, Hkv, Sl, D, generator=g, device=dev).to(torch.bfloat16)
-    v = torch.randn(1, Hkv, Sl, D, generator=g, device=dev).to(torch.bfloat16)
+    if world > 1:
+        # host shards from the seeded generator (the parity check regenerates them)
+        hq, hk, hv = (torch.from_numpy(ring_shard(x, rank, world, S)).to(torch.bfloat16).pin_memory()
+                      for x in ("q", "k", "v"))
+        q, k, v = (t.to(dev) for t in (hq, hk, hv))
+    else:
+        g = torch.Generator(device=dev).manual_seed(11)
+        q = torch.randn(1, Hq, Sl, D, generator=g, device=dev).to(torch.bfloat16)
+        k = torch.randn(1, Hkv, Sl, D, generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn(1, Hkv, Sl, D, generator=g, device=dev).to(torch.bfloat16)
     mod = ax.causal_mod()
     grp = dist.group.WORLD if world > 1 else None
     tm = Timer(torch, dist, world)
+    state = {}
 
     def step(marks):
         with torch.no_grad():
             if world > 1:
-                ring_forward(q, k, v, score_mod=mod, group=grp)
+                state["out"] = ring_forward(q, k, v, score_mod=mod, group=grp)
             else:
-                ax.flash_attention(q, k, v, score_mod=mod)
+                state["out"] = ax.flash_attention(q, k, v, score_mod=mod)
 
     steps = max(2, min(args.steps, 5))
-    ms, _ = tm.run(step, steps, 3)
+    lib = _lib.load()
+    with Clocks(torch.cuda.current_device()) as clk:
+        n0 = lib.attn_launch_count()
+        ms, _ = tm.run(step, steps, 3)
+        launches = (lib.attn_launch_count() - n0) * steps // (steps + 3)
     fl = 4.0 * D * Hq * S * (S + 1) / 2
     tf = fl / (ms * 1e-3) / 1e12
+    line = {"metric": "ring attention tokens/s", "value": round(S / (ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": world, "ms_per_step": round(ms, 3), "tflops_total": round(tf, 2),
+            "tflops_per_gpu": round(tf / world, 2), "scaling": "strong",
+            "config": f"B1 S{S} (S/P={Sl}) Hq{Hq} Hkv{Hkv} D{D} bf16 causal, "
+                      f"{'zig-zag ring over NCCL' if world > 1 else 'one GPU, flash kernel'}"}
+    if world == 1:
+        return line
     # Per-GPU reference for the ring: one GPU's causal flash forward on a
     # sequence of the shard length S/P (same heads), no exchange.
     base = None
-    if world > 1:
-        if rank == 0:
-            t1 = Timer(torch, None, 1)
-            with torch.no_grad():
-                b_ms, _ = t1.run(lambda m: ax.flash_attention(q, k, v, score_mod=mod), steps, 3)
-            base = round(4.0 * D * Hq * Sl * (Sl + 1) / 2 / (b_ms * 1e-3) / 1e12, 2)
-        dist.barrier()
-    return {"metric": "ring attention tokens/s", "value": round(S / (ms * 1e-3), 1), "unit": "tokens/s",
-            "n_gpus": world, "ms_per_step": round(ms, 3), "tflops_total": round(tf, 2),
-            "tflops_per_gpu": round(tf / world, 2), "one_gpu_causal_tflops_at_shard_len": base,
-            "scaling": "strong",
-            "config": f"B1 S{S} (S/P={Sl}) Hq{Hq} Hkv{Hkv} D{D} bf16 causal, "
-                      f"{'zig-zag ring over NCCL' if world > 1 else 'one GPU, flash kernel'}"}
+    if rank == 0:
+        t1 = Timer(torch, None, 1)
+        with torch.no_grad():
+            b_ms, _ = t1.run(lambda m: ax.flash_attention(q, k, v, score_mod=mod), steps, 3)
+        base = round(4.0 * D * Hq * Sl * (Sl + 1) / 2 / (b_ms * 1e-3) / 1e12, 2)
+    dist.barrier()
+    line["one_gpu_causal_tflops_at_shard_len"] = base
+    if not headline:
+        return line
+
+    # e2e through the public API: this rank's q/k/v shard from pinned host
+    # memory in, its output shard back to pinned host memory, every step.
+    bind_axis("bench_sp", grp)
+
+    def e2e_step(tq, tk, tv):
+        with torch.no_grad():
+            return (ax.ring_attention(tq, tk, tv, score_mod=mod, axis_name="bench_sp"),)
+
+    host_out = [torch.empty_like(hq).pin_memory()]
+    e2e_ms = e2e_pipelined(torch, dist, world, dev, (hq, hk, hv), host_out, e2e_step, steps, warmup=2)
+
+    # In-run parity: sampled output rows of this rank's shard against the
+    # oracle over the whole global sequence (all ranks' K/V regenerated here).
+    import oracle as O
+
+    out = state["out"].float().cpu().numpy()
+    kg = np.concatenate([ring_shard("k", r, world, S) for r in range(world)], axis=2)
+    vg = np.concatenate([ring_shard("v", r, world, S) for r in range(world)], axis=2)
+    kg, vg = O.bf16_round(kg), O.bf16_round(vg)
+    qn = hq.float().numpy()
+    rows = np.unique(np.concatenate([[0, 1, Sl // 2, Sl - 1],
+                                     np.random.default_rng(rank).choice(Sl, 12, replace=False)])) + rank * Sl
+    diff = np.zeros(3)  # max-abs, sum |got - want|, sum |want|
+    for h in (0, 13, 31):
+        o, _ = O.gqa_attention_rows(qn, kg, vg, 0, [h], rows, score_mod=O.causal_mod(), q_offset=rank * Sl)
+        got = out[0, h, rows - rank * Sl]
+        d = np.abs(got.astype(np.float64) - o[0])
+        diff += [0.0, d.sum(), np.abs(o[0]).sum()]
+        diff[0] = max(diff[0], d.max())
+    t = torch.tensor(diff, dtype=torch.float64, device=dev)
+    mx = t[:1].clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t)
+    parity = {"max_abs": float(mx.item()), "mean_rel": float(t[1].item() / max(t[2].item(), 1e-30)),
+              "rows_checked": int(len(rows) * 3 * world), "oracle": "O.gqa_attention_rows over the global sequence",
+              "bars": {"max_abs": 2e-2, "mean_rel": 1e-2}}
+    parity["ok"] = parity["max_abs"] <= 2e-2 and parity["mean_rel"] <= 1e-2
+
+    peak_b = peaks["bf16_tflops"]
+    per_gpu = tf / world
+    line.update({
+        "steps": steps, "warmup": 3, "higher_is_better": True, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1) per shard, seeded numpy default_rng",
+        "config": {"workload": line["config"], "batch": 1, "seq_len": S, "seq_per_rank": Sl, "heads_q": Hq,
+                   "heads_kv": Hkv, "head_dim": D, "mask": "causal_mod()",
+                   "parallelism": f"sequence-parallel ring x{world} (zig-zag chunks, NCCL send/recv of K/V)",
+                   "l2": "inputs larger than L2 (q shard >= 128 MiB)"},
+        "roofline": {"kernel": "fwd2::flash_fwd2_kernel<128,bf16> per hop (tcgen05) + ring::lse_merge_kernel",
+                     "bound": "tensor", "achieved": round(per_gpu, 2), "peak": peak_b, "unit": "TFLOP/s",
+                     "frac": round(per_gpu / peak_b, 4), "traffic": None,
+                     "algorithmic_per_step_per_gpu": fl / world},
+        "e2e": {"value": round(S / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": nbytes((hq, hk, hv)) * world, "d2h_bytes_per_step": nbytes(host_out) * world,
+                "returned": "every rank's output shard to pinned host memory every step"},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+        "parity": parity,
+        "peaks_source": PEAKS_SRC,
+    })
+    if base:
+        line["scaling_efficiency_vs_one_gpu_at_shard_len"] = round(per_gpu / base, 4)
+    return line
 
 
 def run_fp32(args, torch, peaks):
@@ -561,6 +688,59 @@ def cpu_cores():
         return os.cpu_count()
 
 
+def run_cpu_ring(world, S_sample=2048):
+    """The oracle's ring recurrence (the reference's per-shard scan, every
+    block computed) over ``world`` shards of a 1-head causal sample; returns
+    algorithmic FLOP/s and the seconds it took."""
+    import oracle as O
+
+    rng = np.random.default_rng(0)
+    q, k, v = (O.bf16_round(rng.standard_normal((1, 1, S_sample, RING["D"]), dtype=np.float32)) for _ in range(3))
+    t0 = time.perf_counter()
+    O.ring_attention_partitioned(q, k, v, world, score_mod=O.causal_mod())
+    dt = time.perf_counter() - t0
+    return 4.0 * RING["D"] * S_sample * (S_sample + 1) / 2 / dt, dt
+
+
+def reference_line(args, world):
+    """``--impl reference``: the CPU restatement of the reference on this
+    host's cores, on bounded samples of the workload our arm reports at this
+    N (the flash step at N=1, the ring at N>1), in the same metric."""
+    common = {"impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+              "higher_is_better": True, "vs_baseline": None, "dtype": "f32",
+              "data": "synthetic N(0,1), seeded numpy default_rng"}
+    if world > 1 and args.workload in ("default", "ring"):
+        S = RING["S"] if args.scale == "full" else 16384
+        run_cpu_ring(world, 512)  # untimed warm-up
+        per = [run_cpu_ring(world) for _ in range(args.steps)]
+        rate = statistics.median(x[0] for x in per)
+        full = 4.0 * RING["D"] * RING["Hq"] * S * (S + 1) / 2
+        v = S / (full / rate)
+        sample = (f"oracle ring_attention_partitioned over {world} shards, 1 head, S=2048 causal, D=128, fp32; "
+                  f"tokens/s of the full config at the sample's algorithmic FLOP rate")
+        line = dict(common, metric="ring attention tokens/s", value=round(v, 4), unit="tokens/s",
+                    ms_per_step=round(statistics.median(x[1] for x in per) * 1e3, 2), scaling="strong",
+                    config={"workload": f"B1 S{S} (S/P={S // world}) Hq{RING['Hq']} Hkv{RING['Hkv']} "
+                                        f"D{RING['D']} bf16 causal, zig-zag ring over NCCL"})
+        unit = "tokens/s"
+    else:
+        run_cpu_flash("arm")  # one untimed warm-up sample
+        per = [run_cpu_flash("arm") for _ in range(args.steps)]
+        v = statistics.median(x[0] for x in per)
+        sample = per[0][2]
+        c = flash_cfg(args.scale)
+        line = dict(common, metric="flash attention fwd+bwd TFLOP/s (algorithmic)", value=round(v, 5),
+                    unit="TFLOP/s", ms_per_step=round(statistics.median(x[1] for x in per) * 1e3, 2),
+                    scaling="weak",
+                    config={"workload": f"flash fwd+bwd B{c['B']} Hq{c['Hq']} Hkv{c['Hkv']} S{c['S']} D{c['D']} "
+                                        f"sliding_window({c['W']})+alibi({c['Hq']})"})
+        unit = "TFLOP/s"
+    line["cpu_baseline"] = {"value": line["value"], "unit": unit, "cores": cpu_cores(), "kind": "port",
+                            "sample": sample}
+    line["e2e"] = {"value": line["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    return line
+
+
 # -------------------------------------------------------------------- main --
 
 PEAKS_SRC = "measured"
@@ -573,8 +753,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["flash", "paged", "kv_cache", "document", "fp32", "ring"],
-                    default="flash")
+    ap.add_argument("--workload", choices=["default", "flash", "paged", "kv_cache", "document", "fp32", "ring"],
+                    default="default")
     ap.add_argument("--scale", choices=["full", "small"], default="full")
     ap.add_argument("--no-secondary", action="store_true")
     args = ap.parse_args()
@@ -587,24 +767,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        per = []
-        run_cpu_flash("arm")  # one untimed warm-up sample
-        for _ in range(args.steps):
-            v, dt, sample = run_cpu_flash("arm")
-            per.append((v, dt))
-        v = statistics.median(x[0] for x in per)
-        ms = statistics.median(x[1] for x in per) * 1e3
-        c = flash_cfg(args.scale)
-        line = {"metric": "flash attention fwd+bwd TFLOP/s (algorithmic)", "value": round(v, 5), "unit": "TFLOP/s",
-                "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f32", "data": "synthetic N(0,1), seeded numpy default_rng",
-                "config": {"workload": f"flash fwd+bwd B{c['B']} Hq{c['Hq']} Hkv{c['Hkv']} S{c['S']} D{c['D']} "
-                                       f"sliding_window({c['W']})+alibi({c['Hq']})"},
-                "cpu_baseline": {"value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
-                                 "sample": sample},
-                "e2e": {"value": round(v, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line))
+        print(json.dumps(reference_line(args, world)))
         return 0
 
     import torch
@@ -616,15 +779,23 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        if args.workload == "flash":
+        if args.workload == "default" and world > 1:
+            # Multi-GPU headline: the sequence-parallel ring (strong scaling).
+            line = run_ring(args, torch, dist, rank, world, peaks, headline=True)
+            if not args.no_secondary:
+                fl = run_flash(args, torch, dist, rank, world, peaks)
+                if rank == 0:
+                    line["secondary"] = {"flash_replicas": {k: fl[k] for k in (
+                        "metric", "value", "unit", "ms_per_step", "fwd_tflops", "bwd_tflops", "scaling", "config")}}
+        elif args.workload in ("default", "flash"):
             line = run_flash(args, torch, dist, rank, world, peaks)
             if rank == 0 and world == 1:
                 v, dt, sample = run_cpu_flash("baseline")
                 line["cpu_baseline"] = {"value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(),
                                         "kind": "port", "sample": sample, "seconds": round(dt, 2)}
-            ring = None if args.no_secondary else run_ring(args, torch, dist, rank, world, peaks)
-            if rank == 0 and not args.no_secondary:
-                line["secondary"] = {"ring": ring, "paged": run_paged(args, torch, peaks),
+            if world == 1 and not args.no_secondary:
+                line["secondary"] = {"ring": run_ring(args, torch, dist, rank, world, peaks),
+                                     "paged": run_paged(args, torch, peaks),
                                      "kv_cache": run_kv_cache(args, torch, peaks),
                                      "document": run_document(args, torch, peaks),
                                      "fp32": run_fp32(args, torch, peaks)}
@@ -637,7 +808,7 @@ def main():
         elif args.workload == "document":
             line = run_document(args, torch, peaks)
         elif args.workload == "ring":
-            line = run_ring(args, torch, dist, rank, world, peaks)
+            line = run_ring(args, torch, dist, rank, world, peaks, headline=world > 1)
         else:
             line = run_fp32(args, torch, peaks)
         if rank == 0:

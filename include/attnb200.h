@@ -133,29 +133,43 @@ int attn_paged_decode(const attn_paged_params_t* p, void* stream);
 /* Allocation-free paged decode.  No counterpart in the reference.  Same
  * inputs, outputs and results as attn_paged_decode, but its split partials
  * live in an 8 MiB array inside the library (one per GPU that loads it,
- * held until exit), so it works for callers that must not allocate device
- * memory: code running while a CUDA graph is being captured, serving loops
- * whose allocator forbids cudaMalloc on the hot path (it synchronises the
- * device), and embedders with a fixed memory budget.  `workspace` is
- * ignored.  The first call on each device looks up the array's device
- * address (cudaGetSymbolAddress), so make that first call before any stream
+ * held until the process exits), so callers that cannot allocate device
+ * memory can still decode: serving loops whose allocator forbids cudaMalloc
+ * on the decode path (it synchronises the device), embedders running inside
+ * a fixed device-memory budget, and plugin hosts that pass a kernel only its
+ * inputs and outputs.  `workspace` is ignored.  The first call on each
+ * device (and in each new context) looks up the array's device address
+ * with cudaGetSymbolAddress, so make that first call before any stream
  * capture.  The split count shrinks to fit the array; requests whose
- * num_seqs * num_heads_q * seq_q * (head_dim + 1) floats exceed 8 MiB are
- * rejected with ATTN_ERR_WORKSPACE.  All calls share the array: calls that
- * overlap on the GPU (different streams, no ordering) race. */
+ * num_seqs * num_heads_q * seq_q * (head_dim + 1) floats exceed 8 MiB
+ * (16256 query rows at head_dim 128) are rejected with ATTN_ERR_WORKSPACE.
+ * All calls share the array: calls that overlap on the GPU (different
+ * streams, no ordering between them) race and corrupt each other. */
 int attn_paged_decode_static(const attn_paged_params_t* p, void* stream);
-/* Contiguous copy of sequence `seq`: keys/values [seq_len, heads_kv, head_dim]. */
+/* Contiguous copy of one sequence: keys/values [seq_len, heads_kv, head_dim]
+ * from the pages block_table_row[0 .. ceil(seq_len / block_size)).  Entries
+ * are read as the reference's pool[block_ids] reads them: negative entries
+ * count from the end of the pool, then indices clamp into [0, num_blocks)
+ * (attn_paged_physical_page).  A seq_len above max_blocks * block_size is
+ * ATTN_ERR_INVALID (gather_kv cannot reshape it either). */
 int attn_paged_gather(attn_dtype_t dtype, const void* key_pool, const void* value_pool,
-                      int32_t block_size, int32_t heads_kv, int32_t head_dim,
-                      const int32_t* block_table_row, int32_t seq_len,
+                      int32_t num_blocks, int32_t block_size, int32_t heads_kv, int32_t head_dim,
+                      const int32_t* block_table_row, int32_t max_blocks, int32_t seq_len,
                       void* keys_out, void* values_out, void* stream);
-/* Writes `chunk` new tokens of sequence `seq` at positions start.. (block
- * table already populated; -1 slots are reported through `bad_slot`). */
-int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool,
+/* Writes `chunk` new tokens of one sequence at positions start.. (block
+ * table already populated).  With bad_slot non-NULL (pre-set to INT32_MAX)
+ * only checks: the lowest logical page that has no table column
+ * (>= max_blocks) or an unallocated entry (-1) is stored there, and nothing
+ * is written; append_kv raises for both before writing.  Pages at or past
+ * num_blocks drop their rows, as JAX's .at[].set drops out-of-bounds
+ * updates. */
+int attn_paged_append(attn_dtype_t dtype, void* key_pool, void* value_pool, int32_t num_blocks,
                       int32_t block_size, int32_t heads_kv, int32_t head_dim,
-                      const int32_t* block_table_row, int32_t start, int32_t chunk,
-                      const void* keys_new, const void* values_new,
-                      int32_t* bad_slot, void* stream);
+                      const int32_t* block_table_row, int32_t max_blocks, int32_t start, int32_t chunk,
+                      const void* keys_new, const void* values_new, int32_t* bad_slot, void* stream);
+/* The pool page a block-table entry selects (host copy of the kernels' rule):
+ * entry < 0 -> entry + num_blocks, then clamped into [0, num_blocks). */
+int64_t attn_paged_physical_page(int32_t entry, int32_t num_blocks);
 
 /* ---- ring attention ------------------------------------------------------ */
 /* Merges one partial attention result into a running one, row by row, by
@@ -193,8 +207,13 @@ typedef struct {
 int attn_rope(const attn_rope_params_t* p, void* stream);
 
 /* ---- diagnostics -------------------------------------------------------- */
-/* Reads and clears the device status word that bounded waits set on
- * timeout (0 = none).  Synchronises the current device. */
+/* Reads and clears the device status words (0 = none).  Synchronises the
+ * current device.  Codes 0x101-0x104: a bounded wait timed out (the kernel
+ * unwound; results are invalid).  0x201: a paged decode met a seq_lengths
+ * entry above max_context and attended only its first splits.  0x202: a
+ * paged decode met a sequence longer than max_blocks_per_seq * block_size
+ * and reused the row's last entry for the pages past it.  A timeout code
+ * takes precedence over a notice. */
 int attn_device_status(int32_t* status);
 const char* attn_status_string(int status);
 int attn_version(void);

@@ -24,7 +24,8 @@ __all__ = [
     "additive_bias_mod", "mask_mod_to_score_mod", "make_padding_mask",
     "make_causal_mask", "make_sliding_window_mask", "make_document_mask",
     "combine_masks", "standard_attention", "standard_attention_lse",
-    "memory_efficient_attention", "attention_rows", "standard_attention_bwd",
+    "memory_efficient_attention", "attention_rows", "gqa_attention_rows", "gqa_kv_rows_grads",
+    "standard_attention_bwd",
     "repeat_kv", "gqa_attention", "gqa_attention_bwd",
     "ring_attention_partitioned", "PagedKVCache", "init_paged_kv_cache",
     "allocate_blocks", "append_kv", "gather_kv", "paged_attention",
@@ -135,13 +136,19 @@ def alibi_slopes(num_heads: int) -> np.ndarray:
 
 
 def alibi_mod(num_heads: int):
-    """``s - m_h * |q - kv|`` (kernels/score_mods.py:48-81)."""
-    slopes = alibi_slopes(num_heads)[None, :, None, None]
+    """``s - m_h * |q - kv|`` (kernels/score_mods.py:48-81).
+
+    The reference broadcasts a ``(1, H, 1, 1)`` slope array against the full
+    head axis; gathering the slopes with ``h_idx`` gives the same values for
+    that index array and also serves score tiles of a subset of heads (the
+    row-sampled checks below pass the real head ids).
+    """
+    slopes = alibi_slopes(num_heads)
 
     def _mod(scores, b_idx, h_idx, q_idx, kv_idx):
         dt = scores.dtype
         dist = np.abs(q_idx.astype(dt) - kv_idx.astype(dt))
-        return scores - slopes.astype(dt) * dist
+        return scores - slopes.astype(dt)[np.asarray(h_idx)] * dist
 
     return _mod
 
@@ -192,8 +199,10 @@ def document_mask_mod(document_ids):
     ids = np.asarray(document_ids, dtype=np.int32)
 
     def _mod(scores, b_idx, h_idx, q_idx, kv_idx):
-        qi = ids[:, q_idx[0, 0, :, 0]]
-        ki = ids[:, kv_idx[0, 0, 0, :]]
+        # Rows of the batches in b_idx (all of them for the full index array).
+        rows = ids[np.asarray(b_idx)[:, 0, 0, 0]]
+        qi = rows[:, q_idx[0, 0, :, 0]]
+        ki = rows[:, kv_idx[0, 0, 0, :]]
         keep = (qi[:, :, None] == ki[:, None, :])[:, None, :, :]
         return np.where(keep, scores, np.finfo(scores.dtype).min)
 
@@ -365,6 +374,120 @@ def attention_rows(query, key, value, rows, *, mask=None, score_mod=None):
     s = _final_scores(q, key, m, score_mod, q_positions=rows)
     p = _softmax(s)
     return np.einsum("bhqk,bhkd->bhqd", p, value).astype(query.dtype)
+
+
+def _mod_tile(score_mod, scores, b, heads, rows, cols):
+    """``score_mod`` on a score tile of batch ``b``, heads ``heads``, global
+    query positions ``rows`` and key positions ``cols``: the index arrays
+    carry those ids, so the tile sees exactly the values the full
+    ``(B, H, Sq, Skv)`` evaluation gives it (kernels/_api.py:115-136).
+    Returns the modified scores and the 0/1 Jacobian of the mod chain
+    (built-in mods are additive or ``where`` selections; see
+    ``_score_jacobian``)."""
+    if score_mod is None:
+        return scores, np.ones(scores.shape, dtype=scores.dtype)
+    b_idx = np.asarray([b], dtype=np.int32)[:, None, None, None]
+    h_idx = np.asarray(heads, dtype=np.int32)[None, :, None, None]
+    q_idx = np.asarray(rows, dtype=np.int32)[None, None, :, None]
+    kv_idx = np.asarray(cols, dtype=np.int32)[None, None, None, :]
+    out = score_mod(scores, b_idx, h_idx, q_idx, kv_idx)
+    z = np.zeros((1, 1) + scores.shape[2:], dtype=np.float64)
+    jac = np.empty(scores.shape, dtype=scores.dtype)
+    for i, h in enumerate(heads):
+        hi = np.asarray([h], dtype=np.int32)[None, :, None, None]
+        f0 = np.asarray(score_mod(z, b_idx, hi, q_idx, kv_idx), dtype=np.float64)
+        f1 = np.asarray(score_mod(z + 1.0, b_idx, hi, q_idx, kv_idx), dtype=np.float64)
+        jac[:, i] = np.rint(f1 - f0)[0, 0]
+    return np.asarray(out, dtype=scores.dtype), jac
+
+
+def gqa_attention_rows(query, key, value, b, heads, rows, *, score_mod=None, d_out=None, q_offset=0):
+    """Exact rows of ``gqa_attention`` (repeat K/V, then ``standard_attention``,
+    kernels/attention.py:54-71 after attention.py:32-39) and, with ``d_out``,
+    the matching rows of its query gradient.
+
+    One output row depends only on its query row and all of K/V, so rows of a
+    shape whose full score matrix does not fit are still exact.  ``b`` is one
+    batch index, ``heads`` query heads, ``rows`` query positions (0-based,
+    global); ``d_out`` is the full upstream gradient (B, Hq, Sq, D).  Returns
+    ``out (len(heads), len(rows), D)``, natural-log ``lse (len(heads),
+    len(rows))`` and, with ``d_out``, ``dq`` of the same shape as ``out``
+    (``dS = P ∘ (dO Vᵀ − rowsum(dO ∘ O))`` masked by the mod Jacobian,
+    ``dQ = scale · dS K``).  ``query``/``d_out`` may hold only the rows from
+    global position ``q_offset`` on (one rank's shard of a sequence whose
+    keys are all given).
+    """
+    rows = np.asarray(rows)
+    hq, hkv = query.shape[1], key.shape[1]
+    grp = hq // hkv
+    dt = query.dtype
+    scale = softmax_scale(query.shape[-1], dt)
+    cols = np.arange(key.shape[2])
+    outs, lses, dqs = [], [], []
+    for h in heads:
+        kh, vh = key[b, h // grp], value[b, h // grp]
+        qr = query[b, h, rows - q_offset]
+        s = (qr @ kh.T * scale)[None, None]
+        s, jac = _mod_tile(score_mod, s, b, [h], rows, cols)
+        s, jac = s[0, 0], jac[0, 0]
+        m = np.max(s, axis=-1, keepdims=True)
+        e = np.exp(s - m)
+        l = np.sum(e, axis=-1, keepdims=True)
+        p = e / l
+        o = p @ vh
+        outs.append(o.astype(dt))
+        lses.append((m + np.log(l))[:, 0])
+        if d_out is not None:
+            dor = d_out[b, h, rows - q_offset]
+            delta = np.sum(dor * o, axis=-1, keepdims=True)
+            ds = p * (dor @ vh.T - delta) * jac
+            dqs.append((ds @ kh * scale).astype(dt))
+    res = (np.stack(outs), np.stack(lses))
+    return res + (np.stack(dqs),) if d_out is not None else res
+
+
+def gqa_kv_rows_grads(query, key, value, d_out, b, hkv, kv_rows, *, score_mod=None, q_block=512,
+                      q_range=None, kv_range=None):
+    """dK and dV rows ``kv_rows`` of kv head ``hkv`` (batch ``b``) of
+    ``gqa_attention``: the gradient autodiff gives through ``jnp.repeat``
+    (attention.py:32-39), i.e. the per-head ``dK = scale · dSᵀ Q``,
+    ``dV = Pᵀ dO`` summed over the query heads sharing the kv head.
+
+    Each query row's softmax needs its whole score row, so the rows are
+    processed in blocks of ``q_block`` against all keys.  ``q_range`` /
+    ``kv_range`` ((lo, hi) positions) restrict the work; the result stays
+    exact when every (q, kv) pair outside them is masked (finfo.min scores
+    contribute exactly 0 to a softmax row that keeps any key).
+    """
+    kv_rows = np.asarray(kv_rows)
+    hq, nh_kv = query.shape[1], key.shape[1]
+    grp = hq // nh_kv
+    dt = query.dtype
+    scale = softmax_scale(query.shape[-1], dt)
+    q_lo, q_hi = q_range if q_range is not None else (0, query.shape[2])
+    k_lo, k_hi = kv_range if kv_range is not None else (0, key.shape[2])
+    cols = np.arange(k_lo, k_hi)
+    kh, vh = key[b, hkv, k_lo:k_hi], value[b, hkv, k_lo:k_hi]
+    sel = kv_rows - k_lo
+    dk = np.zeros((len(kv_rows), key.shape[-1]), dtype=np.float64)
+    dv = np.zeros_like(dk)
+    for h in range(hkv * grp, (hkv + 1) * grp):
+        for r0 in range(q_lo, q_hi, q_block):
+            rows = np.arange(r0, min(q_hi, r0 + q_block))
+            qr, dor = query[b, h, rows], d_out[b, h, rows]
+            s = (qr @ kh.T * scale)[None, None]
+            s, jac = _mod_tile(score_mod, s, b, [h], rows, cols)
+            s, jac = s[0, 0], jac[0, 0]
+            m = np.max(s, axis=-1, keepdims=True)
+            e = np.exp(s - m)
+            p = e / np.sum(e, axis=-1, keepdims=True)
+            o = p @ vh
+            delta = np.sum(dor * o, axis=-1, keepdims=True)
+            ps = p[:, sel]
+            ds = ps * (dor @ vh[sel].T - delta) * jac[:, sel]
+            dv += ps.T.astype(np.float64) @ dor
+            dk += (ds.T.astype(np.float64) @ qr) * scale
+    return dk.astype(dt), dv.astype(dt)
 
 
 def _score_jacobian(q, k, mask, score_mod):

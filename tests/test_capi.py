@@ -68,3 +68,18 @@ def test_ctypes_layout_matches_c_compiler(tmp_path):
         assert int(got[cname]) == ctypes.sizeof(py), cname
         for fname, _ in py._fields_:
             assert int(got[f"{cname}.{fname}"]) == getattr(py, fname).offset, f"{cname}.{fname}"
+
+
+def test_block_table_entries_are_read_like_jax_indexing():
+    """The page rule shared by the gather, append and decode kernels (host copy
+    of the same inline function): a negative entry counts from the end of the
+    pool, then the index is clamped into the pool -- what JAX's pool[block_ids]
+    does in the reference's gather_kv (attnax/paged_cache.py:222-230)."""
+    if not pathlib.Path(_lib.LIB_PATH).exists():
+        pytest.fail("libattnb200.so is not built; run __graft_entry__.build()")
+    page = _lib.load().attn_paged_physical_page
+    nb = 10
+    for entry, want in [(0, 0), (5, 5), (9, 9), (10, 9), (2**31 - 1, 9), (-1, 9), (-10, 0), (-11, 0),
+                        (-(2**31), 0)]:
+        assert page(entry, nb) == want, entry
+    assert page(3, 0) == -1

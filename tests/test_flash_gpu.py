@@ -8,7 +8,7 @@ import torch
 
 import attnax_b200 as ax
 import oracle as O
-from tests._util import assert_bf16_close, assert_fp32_close, randn
+from tests._util import assert_bf16_close, assert_bf16_grad_close, assert_fp32_close, randn
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -176,9 +176,9 @@ def test_backward(dtype, D, mod):
     want = O.gqa_attention_bwd(q, k, v, do, score_mod=m_o)
     for name, got, w in zip(("dq", "dk", "dv"), (tq.grad, tk.grad, tv.grad), want):
         if bf:
-            assert_bf16_close(npy(got), w, f"{mod} {name}", scale_with_max=True)
+            assert_bf16_grad_close(npy(got), w, f"{mod} {name}")
         else:
-            assert_fp32_close(npy(got), w, f"{mod} {name}", atol=2e-4)
+            assert_fp32_close(npy(got), w, f"{mod} {name}")
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -196,7 +196,7 @@ def test_backward_full_tiles(dtype, mod):
     out.backward(T(do, dtype))
     want = O.gqa_attention_bwd(q, k, v, do, score_mod=m_o)
     for name, got, w in zip(("dq", "dk", "dv"), (tq.grad, tk.grad, tv.grad), want):
-        assert_bf16_close(npy(got), w, f"{mod} {name}", scale_with_max=True)
+        assert_bf16_grad_close(npy(got), w, f"{mod} {name}")
 
 
 @pytest.mark.parametrize("layout", ["packed", "interleaved", "short_q"])
@@ -223,7 +223,7 @@ def test_document_mask_many_tiles(layout):
     out.backward(T(do))
     want = O.gqa_attention_bwd(q, k, v, do, score_mod=m_o)
     for name, got, w in zip(("dq", "dk", "dv"), (tq.grad, tk.grad, tv.grad), want):
-        assert_bf16_close(npy(got), w, f"{layout} {name}", scale_with_max=True)
+        assert_bf16_grad_close(npy(got), w, f"{layout} {name}")
 
 
 def test_backward_fully_masked_rows():
@@ -237,7 +237,7 @@ def test_backward_fully_masked_rows():
     out.backward(T(do, torch.float32))
     want = O.standard_attention_bwd(q, k, v, do, mask=mask, score_mod=O.causal_mod())
     for name, got, w in zip(("dq", "dk", "dv"), (tq.grad, tk.grad, tv.grad), want):
-        assert_fp32_close(npy(got), w, name, atol=2e-4)
+        assert_fp32_close(npy(got), w, name)
 
 
 def test_errors_match_reference_behaviour():

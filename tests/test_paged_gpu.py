@@ -125,3 +125,46 @@ def test_decode_with_score_mod_uses_gather_path():
     got = npy(ax.paged_attention(torch.tensor(q, dtype=torch.bfloat16, device=DEV), cache, 0,
                                  score_mod=ax.alibi_mod(4)))
     assert_bf16_close(got, O.paged_attention(q, oc, 0, score_mod=O.alibi_mod(4)), "alibi")
+
+
+def test_minus_one_entries_select_the_last_pool_page():
+    """A -1 entry inside a sequence's length reads the pool's last page, as
+    the reference's pool[block_ids] does (negative ids count from the end)."""
+    rng = np.random.default_rng(40)
+    cache, oc = _random_cache(rng, [70, 40], 8)
+    table = oc.block_table.copy()
+    table[0, 2] = -1
+    table[1, 0] = -1
+    oc = O.PagedKVCache(oc.key_pool, oc.value_pool, table, oc.seq_lengths)
+    cache = ax.PagedKVCache(cache.key_pool, cache.value_pool, torch.tensor(table, device=DEV), cache.seq_lengths)
+    for s in range(2):
+        k, v, _ = ax.gather_kv(cache, s)
+        wk, wv, _ = O.gather_kv(oc, s)
+        np.testing.assert_array_equal(npy(k), wk)
+        np.testing.assert_array_equal(npy(v), wv)
+    q = randn(rng, (2, 32, 1, 128), True)
+    got = npy(ax.paged_attention_batched(torch.tensor(q, dtype=torch.bfloat16, device=DEV), cache))
+    assert_bf16_close(got, O.paged_attention_batched(q, oc), "-1 entries")
+
+
+def test_max_context_below_a_length_is_reported():
+    """max_context is the caller's bound; a longer sequence attends only the
+    splits that bound plans (its first 2048 tokens here) and the decode leaves
+    a notice in the device status instead of failing silently."""
+    from attnax_b200 import _lib
+    from attnax_b200.paged import paged_decode_raw
+
+    rng = np.random.default_rng(41)
+    lens = [5000, 300]
+    cache, oc = _random_cache(rng, lens, 8)
+    _lib.device_status()  # clear
+    q = randn(rng, (2, 32, 1, 128), True)
+    got = npy(paged_decode_raw(torch.tensor(q, dtype=torch.bfloat16, device=DEV), cache, max_context=2048))
+    assert _lib.device_status() == _lib.NOTICE_CONTEXT_OVERRUN
+    assert _lib.device_status() == 0  # read and cleared
+    cut = O.PagedKVCache(oc.key_pool, oc.value_pool, oc.block_table, np.array([2048, 300], np.int32))
+    assert_bf16_close(got, O.paged_attention_batched(q, cut), "first splits only")
+    with pytest.raises(ValueError):
+        ax.paged_attention_batched(torch.tensor(q, dtype=torch.bfloat16, device=DEV),
+                                   ax.PagedKVCache(cache.key_pool, cache.value_pool, cache.block_table[:, :100],
+                                                   cache.seq_lengths))

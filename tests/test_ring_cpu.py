@@ -35,8 +35,10 @@ class OracleOps:
         self.mod, self.mask, self.rep = mod, mask, hq // hkv
         # True when the chain only selects a band (none / causal / window), as
         # KernelOps decides from the tagged mods: the schedule may then batch
-        # fully kept pairs into position-free calls
+        # fully kept pairs into position-free calls (attend_full).  The workers
+        # set it per case and count the batched calls.
         self.position_free = False
+        self.full_calls = 0
 
     def exchange(self, sends, recvs):
         self.x.exchange(sends, recvs)
@@ -67,6 +69,7 @@ class OracleOps:
         return torch.from_numpy(o), torch.from_numpy(lse)
 
     def attend_full(self, q, k, v):
+        self.full_calls += 1
         qn, kn, vn = (t.double().numpy() for t in (q, k, v))
         kn, vn = np.repeat(kn, self.rep, 1), np.repeat(vn, self.rep, 1)
         o, lse = O.standard_attention_lse(qn, kn, vn)
@@ -143,6 +146,14 @@ def _worker(rank, world, port, q, k, v, want):
             out, _ = ring_schedule_forward(tq, tk, tv, ops=ops, sched=sched, band=band)
             np.testing.assert_allclose(out.numpy(), want[case][:, :, sl], atol=1e-10, rtol=1e-10,
                                        err_msg=case)
+            if case == "causal":
+                # zig-zag causal hops whose two kept chunk pairs are whole run as one
+                # batched position-free call (every rank has at least one such hop)
+                assert ops.full_calls > 0, "the batched hop path did not run"
+            if case == "none":
+                # no band: every hop's 4 pairs are kept, none is batched (2 chunks per
+                # rank only under zig-zag)
+                assert ops.full_calls == 0
     finally:
         dist.destroy_process_group()
 

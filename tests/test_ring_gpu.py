@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import oracle as O
-from tests._util import BF16_MAX_ABS, BF16_MEAN_REL, errors
+from tests._util import BF16_MAX_ABS, BF16_MEAN_REL, BF16_STORE_REL, errors
 
 pytestmark = pytest.mark.gpu
 
@@ -72,8 +72,9 @@ def test_ring_two_gpus_matches_global_attention(tmp_path):
     mp.spawn(_worker, args=(2, _free_port(), q, k, v, want, str(tmp_path)), nprocs=2, join=True)
     for r in range(2):
         for line in (tmp_path / f"rank{r}.txt").read_text().splitlines():
-            name, mx, rel = line.split()
-            assert float(mx) <= BF16_MAX_ABS and float(rel) <= BF16_MEAN_REL, f"rank {r} {line}"
+            # |err| - 2^-8 |ref| (bf16 storage rounding of each gradient) within the 2e-2 bar
+            name, excess, rel = line.split()
+            assert float(excess) <= BF16_MAX_ABS and float(rel) <= BF16_MEAN_REL, f"rank {r} {line}"
 
 
 def _bwd_worker(rank, world, port, q, k, v, do, want, result_dir):
@@ -102,9 +103,10 @@ def _bwd_worker(rank, world, port, q, k, v, do, want, result_dir):
             out = ax.ring_attention(tq, tk, tv, score_mod=mod, axis_name="sp")
             out.backward(torch.tensor(np.ascontiguousarray(do[:, :, sl]), dtype=torch.bfloat16, device="cuda"))
             for gname, g, w in zip(("dq", "dk", "dv"), (tq.grad, tk.grad, tv.grad), want[name]):
-                scale = max(1.0, float(np.abs(w).max()))
-                mx, rel = errors(g.float().cpu().numpy() / scale, w[:, :, sl] / scale)
-                lines.append(f"{name}_{gname} {mx} {rel}")
+                got, ref = g.float().cpu().numpy().astype(np.float64), w[:, :, sl].astype(np.float64)
+                _, rel = errors(got, ref)
+                excess = float(np.max(np.abs(got - ref) - BF16_STORE_REL * np.abs(ref)))
+                lines.append(f"{name}_{gname} {excess} {rel}")
         with open(os.path.join(result_dir, f"bwd_rank{rank}.txt"), "w") as f:
             f.write("\n".join(lines))
         dist.barrier()
@@ -127,5 +129,6 @@ def test_ring_two_gpus_backward_matches_global_gradients(tmp_path):
     mp.spawn(_bwd_worker, args=(2, _free_port(), q, k, v, do, want, str(tmp_path)), nprocs=2, join=True)
     for r in range(2):
         for line in (tmp_path / f"bwd_rank{r}.txt").read_text().splitlines():
-            name, mx, rel = line.split()
-            assert float(mx) <= BF16_MAX_ABS and float(rel) <= BF16_MEAN_REL, f"rank {r} {line}"
+            # |err| - 2^-8 |ref| (bf16 storage rounding of each gradient) within the 2e-2 bar
+            name, excess, rel = line.split()
+            assert float(excess) <= BF16_MAX_ABS and float(rel) <= BF16_MEAN_REL, f"rank {r} {line}"
