@@ -11,10 +11,14 @@ their own ``Hkv`` heads rather than repeated to ``Hq``.
 
 For causal masks the work of a contiguous ring is lopsided (rank P-1 attends
 P blocks, rank 0 one), so the shards are re-dealt "zig-zag": the sequence is
-cut into 2P chunks and rank r works on chunks r and 2P-1-r, which gives every
-rank the same number of unmasked chunk pairs at every step.  The re-deal and
-the final return of the outputs are point-to-point copies; results are
-identical, only the order of work changes.
+cut into 2P chunks and every rank works on two chunks whose indices sum to
+2P-1, which gives every rank the same number of unmasked chunk pairs at
+every step.  The pairs are (2r, 2P-1-2r): rank r keeps the first chunk of
+its own shard and swaps its second one with rank P-1-r, so the re-deal is
+one exchange between mirror ranks and the diagonal block of the kept chunk
+can run while it is in flight.  The re-deal and the final return of the
+outputs are point-to-point copies; results are identical, only the order of
+work changes.
 
 ``RingSchedule`` holds the schedule and is independent of the device: it
 calls an ``ops`` object for attention, merging and point-to-point exchange,
@@ -54,13 +58,13 @@ class RingSchedule:
         """Rank that works on chunk ``cid`` during the ring."""
         if not self.zigzag:
             return cid
-        return cid if cid < self.P else 2 * self.P - 1 - cid
+        return cid // 2 if cid % 2 == 0 else (2 * self.P - 1 - cid) // 2
 
     def held(self, rank: int):
         """Chunks rank ``rank`` works on, in its buffer order."""
         if not self.zigzag:
             return [rank]
-        return [rank, 2 * self.P - 1 - rank]
+        return [2 * rank, 2 * self.P - 1 - 2 * rank]
 
     def public(self, rank: int):
         """Chunks rank ``rank`` holds in the public layout, in shard order."""

@@ -516,7 +516,7 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
       if (CfgKV<D, true>::RED &&
           cudaMemsetAsync(dq_acc, 0, (size_t)B * Hq * Sq_pad * D * sizeof(float), st) != cudaSuccess)
         return ATTN_ERR_CUDA;
-      kf<<<grid_kv, kThreads, CfgKV<D, true>::SMEM, st>>>(q64, k128, v128, do64, a);
+      kf<<<grid_kv, CfgKV<D, true>::THREADS, CfgKV<D, true>::SMEM, st>>>(q64, k128, v128, do64, a);
       if (CfgKV<D, true>::RED)
         dq_convert_t_kernel<T, D><<<dim3((Sq + 63) / 64, Hq, B), 256, 0, st>>>(
             dq_acc, reinterpret_cast<T*>(p->dq), p->dq_strides[0], p->dq_strides[1], p->dq_strides[2], Hq, Sq,
@@ -533,7 +533,7 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
   auto kq = dq_kernel<D, BF16>;
   if (!smem_attr_once(kkv, CfgKV<D, false>::SMEM, &attr_dev_kv) || !smem_attr_once(kq, CfgQ<D>::SMEM, &attr_dev_q))
     return ATTN_ERR_CUDA;
-  kkv<<<grid_kv, kThreads, CfgKV<D, false>::SMEM, st>>>(q64, k128, v128, do64, a);
+  kkv<<<grid_kv, CfgKV<D, false>::THREADS, CfgKV<D, false>::SMEM, st>>>(q64, k128, v128, do64, a);
   kq<<<dim3((Sq + QROWS - 1) / QROWS, Hq, B), kThreads, CfgQ<D>::SMEM, st>>>(q128, k64, v64, do128, a);
   return launch_status(3);
 }

@@ -71,6 +71,19 @@ constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
 #ifndef ATTN_BWD_DQ_KT
 #define ATTN_BWD_DQ_KT 128
 #endif
+#ifndef ATTN_BWD_EW_SPLIT
+#define ATTN_BWD_EW_SPLIT 2  // fused dK/dV/dQ kernel: elementwise warps per TMEM lane quarter
+                             // (4 measured 7% slower at B4 Hq32 Hkv8 S8192: the warps are not
+                             // bound by their own elementwise work)
+#endif
+#ifndef ATTN_BWD_FQ_STAGES
+#define ATTN_BWD_FQ_STAGES 3  // fused kernel: Q/dO stages.  A stage is released when its gradient
+                              // GEMMs complete, which is when the S^T GEMM two iterations later is
+                              // due: with 2 stages every iteration waits out a TMA load (traced)
+#endif
+#ifndef ATTN_BWD_DQ_STEPS
+#define ATTN_BWD_DQ_STEPS 1   // fused kernel: 1 = one staged bulk add per tile, else one per column group
+#endif
 constexpr int KT = ATTN_BWD_DQ_KT;  // kv rows per dq iteration (MMA N): 64 or 128
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -124,7 +137,10 @@ struct CfgKV {
   static_assert(!FQ || D == 128, "fused dQ needs M = head dim = 128");
   static constexpr int KCH = D / 64;
   static constexpr bool RED = FQ && ATTN_BWD_DQ_RED != 0;  // no shared-memory staging of dQ^T
-  static constexpr int ST = (FQ && !RED) ? 2 : ATTN_BWD_KV_STAGES;
+  // Q/dO stages in flight.  A stage is released when the gradient GEMMs of its
+  // iteration complete; the fused kernel fits a third stage only with the dQ
+  // staging split into column-group steps (ATTN_BWD_DQ_STEPS).
+  static constexpr int ST = (FQ && !RED) ? ATTN_BWD_FQ_STAGES : ATTN_BWD_KV_STAGES;
   static constexpr int PB = ATTN_BWD_P_BUFS;
   static constexpr int KV_BYTES = KCH * KROWS * 128;  // K or V tile
   static constexpr int QD_BYTES = KCH * QT * 128;     // Q or dO tile
@@ -134,10 +150,29 @@ struct CfgKV {
   static constexpr int OFF_ST = 2 * KV_BYTES;                 // stages: Q, dO, lse2, delta
   static constexpr int OFF_P = OFF_ST + ST * STAGE;           // P^T  [PB][128 kv][64 q] bf16
   static constexpr int OFF_DS = OFF_P + PB * KROWS * 128;     // dS^T [PB][128 kv][64 q] bf16
+  // Elementwise warps per TMEM lane quarter: each takes QT / SPLIT columns of
+  // every q tile.  The fused kernel (V in TMEM, staged dQ) splits the columns
+  // ATTN_BWD_EW_SPLIT ways; the other variants two ways.
+  static constexpr bool FQ_STAGED = FQ && !RED && ATTN_BWD_FQ_V_TMEM != 0;
+  static constexpr int SPLIT = FQ_STAGED ? ATTN_BWD_EW_SPLIT : 2;
+  static_assert(SPLIT == 2 || SPLIT == 4, "elementwise split");
+  static constexpr int EW_WARPS = 4 * SPLIT;
+  static constexpr int THREADS = (EW_WARPS + 2) * 32;  // + TMA warp + MMA warp
+  static constexpr int HC = QT / SPLIT;                // columns per elementwise thread
   static constexpr int OFF_COLV = OFF_DS + PB * KROWS * 128;  // per elementwise warp: 32 column terms
-  static constexpr int OFF_DQS = OFF_COLV + 8 * 32 * 4;        // fused dQ staging [QT q][D] fp32
-  static constexpr int DQS_BYTES = (FQ && !RED) ? QT * D * 4 : 0;
-  static constexpr int OFF_BAR = OFF_DQS + DQS_BYTES;
+  // Fused dQ staging [QT / DQ_STEPS q][D] fp32: with one step every column
+  // group stages its q rows and one bulk add covers the tile; with SPLIT
+  // steps the groups take turns on a buffer of HC rows.
+  static constexpr int DQ_STEPS = ATTN_BWD_DQ_STEPS == 1 ? 1 : SPLIT;
+  static constexpr int DQ_ROWS = QT / DQ_STEPS;
+  // With V in TMEM its shared-memory tile is dead once the elementwise warps
+  // have copied it (before the MMA warp issues anything), so the one-step
+  // staging buffer (QT x D fp32 = one V tile) reuses it.
+  static constexpr bool DQS_IN_V = FQ_STAGED && DQ_STEPS == 1 && QT * D * 4 <= KV_BYTES;
+  static constexpr int OFF_DQS_OWN = OFF_COLV + EW_WARPS * 32 * 4;
+  static constexpr int OFF_DQS = DQS_IN_V ? OFF_V : OFF_DQS_OWN;
+  static constexpr int DQS_BYTES = (FQ && !RED && !DQS_IN_V) ? DQ_ROWS * D * 4 : 0;
+  static constexpr int OFF_BAR = OFF_DQS_OWN + DQS_BYTES;
   static constexpr int NBAR = 1 + 2 * ST + 2 + 2 + 1 + PB + 1 + 1 + 6;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
@@ -159,7 +194,7 @@ struct CfgKV {
 };
 
 template <int D, bool BF16, bool FQ>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const __grid_constant__ Args a) {
@@ -198,21 +233,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < NSB; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 8);  // one arrival per elementwise warp
+      mbar_init(s_free(i), C::EW_WARPS);  // one arrival per elementwise warp
     }
-    mbar_init(p_full, 8);
+    mbar_init(p_full, C::EW_WARPS);
     for (int q = 0; q < C::PB; ++q) mbar_init(p_free(q), 1);
     mbar_init(acc_done, 1);
-    mbar_init(kv_tmem, 8);
+    mbar_init(kv_tmem, C::EW_WARPS);
     for (int x = 0; x < 2; ++x) {
       mbar_init(dq_full(x), 1);
-      mbar_init(dq_free(x), 8);
+      mbar_init(dq_free(x), C::EW_WARPS);
     }
-    mbar_init(stage_full, 8);
+    mbar_init(stage_full, C::EW_WARPS / C::DQ_STEPS);  // the warps staging one step
     mbar_init(stage_free, 1);
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == C::EW_WARPS + 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -242,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (g, qt) advance of the flat (g, q tile) loop.
 #define DKDV_NEXT(g, qt) ((qt) + 1 == t_hi ? ((qt) = t_lo, ++(g)) : ++(qt))
 
-  if (warp == 8) {
+  if (warp == C::EW_WARPS) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -271,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++i;
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == C::EW_WARPS + 1) {
     if (lane == 0) {
       constexpr int FMT = BF16 ? 1 : 0;
       constexpr uint32_t ID_S = idesc_f16(128, QT, FMT, 0, 0);
@@ -349,9 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && i > 0) ok = issue_grads(i - 1);
       umma_commit(acc_done);
     }
-  } else if (warp < 8) {
+  } else if (warp < C::EW_WARPS) {
     const int r = threadIdx.x & 127;  // kv row within the tile == TMEM lane
-    const int half = warp >> 2;       // columns [32*half, 32*half + 32) of each q tile
+    const int half = warp >> 2;       // columns [HC*half, HC*half + HC) of each q tile
+    constexpr int HC = C::HC;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     uint8_t* PT = sp + C::OFF_P;
     uint8_t* DST = sp + C::OFF_DS;
@@ -367,17 +403,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     if (C::V_TMEM) {
       // Warps 0-3 store their K row, warps 4-7 their V row, into TMEM as bf16
-      // pairs; with V alone in TMEM the two halves store 64-column chunks of V.
+      // pairs; with V alone in TMEM each of the SPLIT column groups stores
+      // 64 / SPLIT packed columns (128 / SPLIT features) of its V row.
       ok = __all_sync(0xffffffffu, mbar_wait(kv_full, 0, kStatusTimeoutSoftmax));
       if (ok && !C::KV_TMEM) {
-        const uint8_t* src = sp + C::OFF_V + half * KROWS * 128;
-        uint32_t w[32];
+        constexpr int PC = 64 / C::SPLIT;  // packed columns per group
+        const int gb = half * PC * 4;      // first byte of the group within the V row
+        const uint8_t* src = sp + C::OFF_V + (gb / 128) * KROWS * 128;
+        uint32_t w[PC];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint4 v = *reinterpret_cast<const uint4*>(src + r * 128 + ((u ^ (r & 7)) << 4));
+        for (int u = 0; u < PC / 4; ++u) {
+          const int unit = (gb % 128) / 16 + u;
+          const uint4 v = *reinterpret_cast<const uint4*>(src + r * 128 + ((unit ^ (r & 7)) << 4));
           w[u * 4 + 0] = v.x; w[u * 4 + 1] = v.y; w[u * 4 + 2] = v.z; w[u * 4 + 3] = v.w;
         }
-        tmem_st32(tmem + lane_base + C::COL_V + half * 32, w);
+        tmem_st_cols<PC>(tmem + lane_base + C::COL_V + half * PC, w);
         tmem_wait_st();
       } else if (ok) {
         const uint8_t* src = sp + (half ? C::OFF_V : C::OFF_K);
@@ -397,44 +437,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_warp(kv_tmem);
     }
     // Fused dQ: tile j's dQ^T (this thread: head-dim row r, q columns
-    // [32*half, 32*half + 32)) -> staging [q][D] fp32 -> one bulk add of the
+    // [HC*half, HC*half + HC)) -> staging [q][D] fp32 -> one bulk add of the
     // whole [QT][D] block into dq_acc by thread 0.
     float* stg = reinterpret_cast<float*>(sp + C::OFF_DQS);
     auto flush_dq = [&](int j, int hq_j, int q0_j) -> bool {
       if (!__all_sync(0xffffffffu, mbar_wait(dq_full(j % C::NDQ), (j / C::NDQ) & 1, kStatusTimeoutSoftmax)))
         return false;
       tc_fence_after();
-      uint32_t v[32];
-      tmem_ld32(tmem + lane_base + C::COL_DQ + (j % C::NDQ) * QT + half * 32, v);
+      uint32_t v[HC];
+      tmem_ld_cols<HC>(tmem + lane_base + C::COL_DQ + (j % C::NDQ) * QT + half * HC, v);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive_warp(dq_free(j % C::NDQ));
       if constexpr (C::RED) {
-        // dq_acc is [B][Hq][D][Sq_pad]: this thread's 32 q values are contiguous.
-        float* dst = a.dq_acc + (((long long)b * a.Hq + hq_j) * D + r) * a.Sq_pad + q0_j + half * 32;
+        // dq_acc is [B][Hq][D][Sq_pad]: this thread's HC q values are contiguous.
+        float* dst = a.dq_acc + (((long long)b * a.Hq + hq_j) * D + r) * a.Sq_pad + q0_j + half * HC;
 #pragma unroll
-        for (int m = 0; m < 8; ++m)
+        for (int m = 0; m < HC / 4; ++m)
           atomicAdd(reinterpret_cast<float4*>(dst + 4 * m),
                     make_float4(__uint_as_float(v[4 * m]), __uint_as_float(v[4 * m + 1]),
                                 __uint_as_float(v[4 * m + 2]), __uint_as_float(v[4 * m + 3])));
         return true;
       }
-      if (threadIdx.x == 0) {
-        bulk_wait_read_all();  // the reduction of tile j - 1 has read the staging buffer
-        mbar_arrive(stage_free);
-      }
-      if (!__all_sync(0xffffffffu, mbar_wait(stage_free, j & 1, kStatusTimeoutSoftmax))) return false;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) stg[(half * 32 + c) * D + r] = __uint_as_float(v[c]);
-      fence_proxy_async_smem();
-      mbar_arrive_warp(stage_full);
+      // Staging [DQ_ROWS q][D]: in step h the column groups whose q rows fall
+      // in [h*DQ_ROWS, (h+1)*DQ_ROWS) write them and thread 0 adds the buffer
+      // into dq_acc once the previous bulk reduction has read it.  Every warp
+      // waits every step's stage_free phase in order (a parity wait cannot
+      // tell a phase from the one two before it, so no waiter may skip one).
       bool ok0 = true;
-      if (threadIdx.x == 0) {
-        ok0 = mbar_wait(stage_full, j & 1, kStatusTimeoutSoftmax);
-        if (ok0) {
-          bulk_reduce_add_f32(a.dq_acc + (((long long)b * a.Hq + hq_j) * a.Sq_pad + q0_j) * D, smem_u32(stg),
-                              QT * D * 4);
-          bulk_commit();
+      for (int h = 0; h < C::DQ_STEPS; ++h) {
+        const uint32_t ph = (uint32_t)(j * C::DQ_STEPS + h) & 1u;
+        if (threadIdx.x == 0) {
+          bulk_wait_read_all();  // the previous reduction has read the staging buffer
+          mbar_arrive(stage_free);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(stage_free, ph, kStatusTimeoutSoftmax))) return false;
+        const int row0 = half * HC - h * C::DQ_ROWS;  // this group's first row in the buffer
+        if (row0 >= 0 && row0 < C::DQ_ROWS) {
+#pragma unroll
+          for (int c = 0; c < HC; ++c) stg[(row0 + c) * D + r] = __uint_as_float(v[c]);
+          fence_proxy_async_smem();
+          mbar_arrive_warp(stage_full);
+        }
+        if (threadIdx.x == 0 && ok0) {
+          ok0 = mbar_wait(stage_full, ph, kStatusTimeoutSoftmax);
+          if (ok0) {
+            bulk_reduce_add_f32(
+                a.dq_acc + (((long long)b * a.Hq + hq_j) * a.Sq_pad + q0_j + h * C::DQ_ROWS) * D,
+                smem_u32(stg), C::DQ_ROWS * D * 4);
+            bulk_commit();
+          }
         }
       }
       return __all_sync(0xffffffffu, ok0);  // warp-uniform
@@ -448,10 +500,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full(i % NSB), (i / NSB) & 1, kStatusTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-      constexpr int HC = QT / 2;  // columns per thread
       float sc[HC], dp[HC];
-      tmem_ld32(tmem + lane_base + C::COL_S + (i % NSB) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(sc));
-      tmem_ld32(tmem + lane_base + C::COL_DP + (i % NSB) * QT + half * HC, *reinterpret_cast<uint32_t(*)[32]>(dp));
+      tmem_ld_cols<HC>(tmem + lane_base + C::COL_S + (i % NSB) * QT + half * HC, reinterpret_cast<uint32_t*>(sc));
+      tmem_ld_cols<HC>(tmem + lane_base + C::COL_DP + (i % NSB) * QT + half * HC, reinterpret_cast<uint32_t*>(dp));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive_warp(s_free(i % NSB));
@@ -461,10 +512,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (st == kFull && fast_mask) {
         // (a full tile has all KROWS kv rows inside the sequence; q columns
         // past the end carry lse2 = +inf and delta = 0, so P = dS = 0 there)
-        static_assert(HC == 32, "one column term per lane");
+        static_assert(HC <= 32, "one column term per lane");
         const float slope = a.mask.alibi_slopes ? __ldg(a.mask.alibi_slopes + hq) * kLog2e : 0.f;
         __syncwarp();
-        colv[lane] = fmaf(-slope, (float)lane, -sl[lane]);
+        if (lane < HC) colv[lane] = fmaf(-slope, (float)lane, -sl[lane]);
         __syncwarp();
         const float base = -slope * (float)clamp_i32(a.mask.q_offset + c0 - kg_row);
         const unsigned long long base2 = f2_pack(base, base);
@@ -543,8 +594,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         T* dst = which ? dkr : dvr;
         const uint32_t col = which ? C::COL_DK : C::COL_DV;
         const float mul = which ? a.scale : 1.f;
+        constexpr int CPP = (D / 32) / C::SPLIT;  // 32-column chunks of dV / dK per column group
+        static_assert(CPP >= 1, "epilogue chunks");
 #pragma unroll
-        for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
+        for (int c = half * CPP; c < (half + 1) * CPP; ++c) {
           uint32_t o[32];
           if (i > 0) {
             tmem_ld32(tmem + lane_base + col + c * 32, o);
@@ -570,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == C::EW_WARPS + 1) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
