@@ -1,8 +1,9 @@
 """Generates the golden vectors in this folder from the reference's own source.
 
-Run from the repository root where the attnax reference checkout is present:
+Run from the repository root, pointing ``--ref`` at a checkout of the attnax
+reference (the directory that contains the ``attnax`` package):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <attnax checkout>
 
 The reference's hot-path modules (``attnax/kernels/*.py``,
 ``attnax/paged_cache.py``, ``attnax/masking.py``, ``attnax/cache.py``,
@@ -105,7 +106,7 @@ def A(x):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="attnax checkout (the directory holding the attnax package)")
     ap.add_argument("--only", choices=["kvcache", "rope"], default=None,
                     help="write only this fixture (leaves the other files untouched)")
     args = ap.parse_args()
