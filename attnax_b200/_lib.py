@@ -80,6 +80,29 @@ class RopeParams(C.Structure):
     ]
 
 
+class RingParams(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int), ("batch", i32), ("num_heads_q", i32), ("num_heads_kv", i32),
+        ("seq_local", i32), ("head_dim", i32), ("q", vp), ("k", vp), ("v", vp), ("out", vp),
+        ("lse", vp), ("softmax_scale", f32), ("has_band", i32), ("band_lo", i64), ("band_hi", i64),
+        ("alibi_slopes", vp), ("zigzag", i32), ("workspace", vp), ("workspace_bytes", szt),
+    ]
+
+
+class RingBwdParams(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int), ("batch", i32), ("num_heads_q", i32), ("num_heads_kv", i32),
+        ("seq_local", i32), ("head_dim", i32), ("q", vp), ("k", vp), ("v", vp), ("out", vp),
+        ("lse", vp), ("d_out", vp), ("dq", vp), ("dk", vp), ("dv", vp), ("softmax_scale", f32),
+        ("has_band", i32), ("band_lo", i64), ("band_hi", i64), ("alibi_slopes", vp), ("zigzag", i32),
+        ("workspace", vp), ("workspace_bytes", szt),
+    ]
+
+
+COMM_ID_BYTES = 128
+RING_PLAN_FIELDS = ("hop", "q_slot", "q_chunks", "kv_slot", "kv_chunks", "q_start", "kv_start", "masked",
+                    "final_from", "local")
+
 # Every symbol the header declares, with its ctypes signature.
 SIGNATURES = {
     "attn_fwd_workspace_size": (szt, [C.POINTER(FwdParams)]),
@@ -94,6 +117,14 @@ SIGNATURES = {
     "attn_paged_physical_page": (i64, [i32, i32]),
     "attn_lse_merge": (C.c_int, [C.c_int, i64, i32, vp, vp, vp, vp, vp, vp]),
     "attn_rope": (C.c_int, [C.POINTER(RopeParams), vp]),
+    "attn_comm_unique_id": (C.c_int, [vp, szt]),
+    "attn_comm_init": (C.c_int, [C.POINTER(vp), i32, i32, vp, szt]),
+    "attn_comm_destroy": (C.c_int, [vp]),
+    "attn_ring_plan": (C.c_int, [i32, i32, i32, i32, i32, i64, i64, i32, C.POINTER(i64), i32]),
+    "attn_ring_fwd_workspace_size": (szt, [C.POINTER(RingParams), i32]),
+    "attn_ring_fwd": (C.c_int, [C.POINTER(RingParams), vp, vp, vp]),
+    "attn_ring_bwd_workspace_size": (szt, [C.POINTER(RingBwdParams), i32]),
+    "attn_ring_bwd": (C.c_int, [C.POINTER(RingBwdParams), vp, vp, vp]),
     "attn_device_status": (C.c_int, [C.POINTER(i32)]),
     "attn_status_string": (C.c_char_p, [C.c_int]),
     "attn_version": (C.c_int, []),

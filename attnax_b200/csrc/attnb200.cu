@@ -216,9 +216,16 @@ static int launch_simt_fwd(const attn_fwd_params_t* p, float* lse, cudaStream_t 
   return launch_status();
 }
 
+// Accumulation target of a ring step (see fwd2::Args::acc_o); null for a plain forward.
+struct RingAcc {
+  float* o;
+  float* lse;
+  int rows, row0, final_from;
+};
+
 template <int D, bool BF16>
 static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2* dq_t, const int2* dkv_t,
-                             const int2* djr, cudaStream_t st) {
+                             const int2* djr, cudaStream_t st, const RingAcc* acc = nullptr) {
   CUtensorMap tq, tk, tv;
   if (!make_tmap(&tq, p->dtype, p->q, p->batch, p->num_heads_q, p->seq_q, D, p->q_strides, fwd2::BM) ||
       !make_tmap(&tk, p->dtype, p->k, p->batch, p->num_heads_kv, p->seq_kv, D, p->k_strides, fwd2::BN) ||
@@ -235,19 +242,24 @@ static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2*
   a.doc_q_tiles = dq_t; a.doc_kv_tiles = dkv_t; a.doc_jrange = djr;
   a.nq_doc = (p->seq_q + kDocTile - 1) / kDocTile;
   a.nk_doc = (p->seq_kv + kDocTile - 1) / kDocTile;
+  a.acc_o = acc ? acc->o : nullptr;
+  a.acc_lse = acc ? acc->lse : nullptr;
+  a.acc_rows = acc ? acc->rows : 0;
+  a.acc_row0 = acc ? acc->row0 : 0;
+  a.acc_final_from = acc ? acc->final_from : 0;
   constexpr int smem = fwd2::Cfg<D>::SMEM;
-  auto kern = fwd2::flash_fwd2_kernel<D, BF16>;
-  static int attr_dev = -1;
+  auto kern = acc ? fwd2::flash_fwd2_kernel<D, BF16, true> : fwd2::flash_fwd2_kernel<D, BF16, false>;
+  static int attr_dev[2] = {-1, -1};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (attr_dev != dev) {
+  if (attr_dev[acc ? 1 : 0] != dev) {
     // The in-kernel register split assumes this exact launch register count.
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != fwd2::kLaunchRegs)
       return ATTN_ERR_UNSUPPORTED;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return ATTN_ERR_CUDA;
-    attr_dev = dev;
+    attr_dev[acc ? 1 : 0] = dev;
   }
   dim3 grid(a.n_ctas, p->num_heads_q, p->batch);
   kern<<<grid, fwd2::kThreads, smem, st>>>(tq, tk, tv, a);
@@ -843,6 +855,7 @@ int attn_paged_decode(const attn_paged_params_t* p, void* stream) {
 
 #include "paged_static.cu"
 #include "rope.cu"
+#include "ring_host.cu"
 
 extern "C" int attn_lse_merge(attn_dtype_t dtype, int64_t rows, int32_t head_dim, float* o_acc,
                               float* lse_acc, const void* o_part, const float* lse_part, void* out,

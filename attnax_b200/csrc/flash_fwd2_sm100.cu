@@ -80,6 +80,17 @@ struct Args {
   const int2* doc_kv_tiles;
   const int2* doc_jrange;  // per q tile: kv tiles whose document ids can match (or null)
   int nq_doc, nk_doc;
+  // Ring accumulation (acc_o non-null): the launch's normalised rows are
+  // folded into a running result by log-sum-exp (the per-step update of
+  // ring_attention, attnax/kernels/attention.py:662-671) instead of being
+  // stored.  acc_o is [B][Hq][acc_rows][D] fp32, acc_lse [B][Hq][acc_rows]
+  // (natural log, -inf = nothing yet; acc_o rows are then not read); launch
+  // row r is accumulator row acc_row0 + r.  Rows >= acc_final_from write the
+  // merged row to `out` (in the tensor dtype) instead of acc_o; the merged
+  // LSE always goes to acc_lse.
+  float* acc_o;
+  float* acc_lse;
+  int acc_rows, acc_row0, acc_final_from;
 };
 
 // Cubic fit of 2^f on [-1/2, 1/2] (max relative error 7.6e-5), our own fit.
@@ -91,7 +102,9 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return __int_as_float(__float_as_int(p) + ((__float_as_int(y) - 0x4B400000) << 23));
 }
 
-template <int D, bool BF16>
+// ACC: the ring variant that merges into a running result (Args::acc_o); a
+// separate instantiation so the plain forward's epilogue stays as it is.
+template <int D, bool BF16, bool ACC = false>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Args a) {
@@ -477,7 +490,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // ------------------------------------------------------------ epilogue --
     if (ok && i > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done(x), (i - 1) & 1, kStatusTimeoutSoftmax));
-    if (ok && my_act) {
+    if (ACC && ok && my_act) {
+      // ---- ring accumulation: merge this launch's row into the running one ----
+      tc_fence_after();
+      const bool row_ok = (my_q0 + r) < a.Sq;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const float lp = (m_run == -FLT_MAX || l_run <= 0.f) ? -INFINITY : (m_run + lg2(l_run)) * kLn2;
+      const long long arow = ((long long)b * a.Hq + hq) * a.acc_rows + a.acc_row0 + my_q0 + r;
+      const float la = row_ok ? a.acc_lse[arow] : -INFINITY;
+      const float mm = fmaxf(la, lp);
+      float ca = 1.f, cp = 0.f, lnew = la;
+      if (mm != -INFINITY) {
+        const float wa = la == -INFINITY ? 0.f : ex2((la - mm) * kLog2e);
+        const float wp = lp == -INFINITY ? 0.f : ex2((lp - mm) * kLog2e);
+        const float tot = wa + wp;
+        ca = wa / tot;
+        cp = wp / tot * inv;
+        lnew = mm + lg2(tot) * kLn2;
+      }
+      const bool read_acc = la != -INFINITY;
+      const bool fin = (my_q0 + r) >= a.acc_final_from;
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* orow = reinterpret_cast<T*>(a.out) + (long long)b * a.o_s0 + (long long)hq * a.o_s1 +
+                (long long)(my_q0 + r) * a.o_s2;
+      float* arow_o = a.acc_o + arow * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (i > 0) {
+          tmem_ld32(tmem + lane_base + C::o_col(x) + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (!row_ok) continue;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          float4 av = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (read_acc) av = *reinterpret_cast<const float4*>(arow_o + c * 32 + v * 4);
+          const float m0 = ca * av.x + cp * __uint_as_float(o[v * 4 + 0]);
+          const float m1 = ca * av.y + cp * __uint_as_float(o[v * 4 + 1]);
+          const float m2 = ca * av.z + cp * __uint_as_float(o[v * 4 + 2]);
+          const float m3 = ca * av.w + cp * __uint_as_float(o[v * 4 + 3]);
+          if (fin) {
+            uint2 w;
+            w.x = pack2(m0, m1, BF16);
+            w.y = pack2(m2, m3, BF16);
+            *reinterpret_cast<uint2*>(orow + c * 32 + v * 4) = w;
+          } else {
+            *reinterpret_cast<float4*>(arow_o + c * 32 + v * 4) = make_float4(m0, m1, m2, m3);
+          }
+        }
+      }
+      if (row_ok) a.acc_lse[arow] = lnew;
+    } else if (ok && my_act) {
       tc_fence_after();
       const bool row_ok = (my_q0 + r) < a.Sq;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;

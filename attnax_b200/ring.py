@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import torch
 
+from . import _ring_capi
 from .flash import _output_dropout, attention
 
 _AXES = {}
@@ -76,6 +77,14 @@ def _ring_run(query, key, value, score_mod, mask, group, zigzag, state):
         zigzag = band is not None and band[0] >= 0 and world > 1
     sched = RingSchedule(world, rank, S, zigzag)
     ops = KernelOps(group, score_mod, mask, B, Hq, S, query.device)
+    if world > 1 and _ring_capi.eligible(query, key, value, score_mod, mask) and (
+            band is None or band[0] <= 0 <= band[1]):
+        # Position-only chains: the whole ring runs in the library (attn_ring_fwd).
+        out, lse = _ring_capi.ring_fwd(query, key, value, score_mod, group, zigzag=sched.zigzag)
+        if state is not None:
+            state.update(public=True, q=query.contiguous(), k=key.contiguous(), v=value.contiguous(), out=out,
+                         lse=lse, sched=sched, ops=ops, band=band, empty=False, score_mod=score_mod, group=group)
+        return out
     out, acc = ring_schedule_forward(query.contiguous(), key.contiguous(), value.contiguous(),
                                      ops=ops, sched=sched, band=band, state=state)
     empty = may_empty_rows(score_mod, mask)
@@ -99,6 +108,14 @@ class _RingFn(torch.autograd.Function):
         from ._ring_impl import ring_schedule_backward
 
         st = ctx.st
+        if st.get("public"):
+            # the library ran the forward ring; its backward ring (attn_ring_bwd)
+            # takes the same public-layout shards
+            dq, dk, dv = _ring_capi.ring_bwd(st["q"], st["k"], st["v"], st["out"], st["lse"], dout,
+                                             st["score_mod"], st["group"], st["sched"].zigzag)
+            ctx.st = None
+            tq, tk, tv = ctx.dtypes
+            return dq.to(tq), dk.to(tk), dv.to(tv), None, None, None, None
         dq, dk, dv = ring_schedule_backward(st["q"], st["k"], st["v"], st["out"], st["lse"],
                                             dout.to(st["q"].dtype).contiguous(), ops=st["ops"],
                                             sched=st["sched"], band=st["band"], empty_rows=st["empty"])

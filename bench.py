@@ -604,7 +604,7 @@ def run_ring(args, torch, dist, rank, world, peaks, headline=False):
                    "heads_kv": Hkv, "head_dim": D, "mask": "causal_mod()",
                    "parallelism": f"sequence-parallel ring x{world} (zig-zag chunks, NCCL send/recv of K/V)",
                    "l2": "inputs larger than L2 (q shard >= 128 MiB)"},
-        "roofline": {"kernel": "fwd2::flash_fwd2_kernel<128,bf16> per hop (tcgen05) + ring::lse_merge_kernel",
+        "roofline": {"kernel": "attn_ring_fwd: fwd2::flash_fwd2_kernel<128,bf16> per chunk pair, LSE merge in its epilogue",
                      "bound": "tensor", "achieved": round(per_gpu, 2), "peak": peak_b, "unit": "TFLOP/s",
                      "frac": round(per_gpu / peak_b, 4), "traffic": None,
                      "algorithmic_per_step_per_gpu": fl / world},

@@ -183,6 +183,81 @@ int64_t attn_paged_physical_page(int32_t entry, int32_t num_blocks);
 int attn_lse_merge(attn_dtype_t dtype, int64_t rows, int32_t head_dim, float* o_acc, float* lse_acc,
                    const void* o_part, const float* lse_part, void* out, void* stream);
 
+/* ---- ring attention over NCCL (one process per GPU) ----------------------- */
+/* Replaces ring_attention (attnax/kernels/attention.py:540-691) run under
+ * shard_map/pmap with axis_name bound: each rank passes its contiguous
+ * shard of the global sequence and gets its output shard back.  NCCL is
+ * loaded at run time (libnccl.so.2).  A communicator is made once per group:
+ * one rank calls attn_comm_unique_id and hands the ATTN_COMM_ID_BYTES bytes
+ * to every rank (the host framework's own broadcast), then every rank calls
+ * attn_comm_init with its device current. */
+#define ATTN_COMM_ID_BYTES 128
+typedef struct attn_comm_s* attn_comm_t;
+int attn_comm_unique_id(void* id, size_t bytes);
+int attn_comm_init(attn_comm_t* comm, int32_t world, int32_t rank, const void* id, size_t bytes);
+int attn_comm_destroy(attn_comm_t comm);
+
+/* The ring's launch plan for one rank (no GPU work; used by tests and
+ * tools): writes up to max_launches records of 10 int64 each --
+ * hop, q_slot, q_chunks, kv_slot, kv_chunks, q_start, kv_start, masked,
+ * final_from, local -- and returns the number of launches (or -status).
+ * Slots index the rank's ring buffer in chunks of C = seq_local / 2 rows
+ * (zigzag) or seq_local rows. */
+int attn_ring_plan(int32_t world, int32_t rank, int32_t seq_local, int32_t zigzag, int32_t has_band,
+                   int64_t band_lo, int64_t band_hi, int32_t position_free, int64_t* launches,
+                   int32_t max_launches);
+
+typedef struct {
+  attn_dtype_t dtype;            /* bf16 or f16 */
+  int32_t batch, num_heads_q, num_heads_kv, seq_local, head_dim;  /* head_dim 64 or 128 */
+  const void* q;                 /* [batch, heads_q, seq_local, head_dim] contiguous: this rank's shard */
+  const void* k;                 /* [batch, heads_kv, seq_local, head_dim] contiguous */
+  const void* v;
+  void* out;                     /* like q; must not alias q, k, v */
+  float* lse;                    /* [batch, heads_q, seq_local] natural log, or NULL */
+  float softmax_scale;
+  /* selection on global positions: keep band_lo <= q - kv <= band_hi
+   * (causal_mod: 0..INT64_MAX; sliding_window_mod(W): 0..W-1; non-causal
+   * window: -(W-1)..W-1); band_lo <= 0 <= band_hi is required */
+  int32_t has_band;
+  int64_t band_lo, band_hi;
+  const float* alibi_slopes;     /* [heads_q] or NULL (alibi_mod) */
+  int32_t zigzag;                /* 1: balanced chunk assignment (causal bands; even seq_local) */
+  void* workspace; size_t workspace_bytes;
+} attn_ring_params_t;
+
+size_t attn_ring_fwd_workspace_size(const attn_ring_params_t* p, int32_t world);
+/* Enqueues the whole ring on compute_stream (attention) and comm_stream
+ * (NCCL); the results are ready in stream order of compute_stream.  Every
+ * rank of the communicator must call it with the same shapes and band. */
+int attn_ring_fwd(const attn_ring_params_t* p, attn_comm_t comm, void* compute_stream, void* comm_stream);
+
+/* Gradients of attn_ring_fwd (the reference differentiates its lax.scan /
+ * ppermute ring with JAX autodiff).  The K/V shards travel the ring again;
+ * every kept chunk pair gives exact partial gradients from the saved global
+ * LSE, dQ accumulates in place and dK/dV accumulate in fp32 buffers that
+ * follow their K/V one hop behind the attention, so the last exchange
+ * brings every rank its own dK/dV.  Same shapes, band and zigzag as the
+ * forward call whose `out` and `lse` are passed here. */
+typedef struct {
+  attn_dtype_t dtype;
+  int32_t batch, num_heads_q, num_heads_kv, seq_local, head_dim;
+  const void* q; const void* k; const void* v;   /* this rank's shards, contiguous */
+  const void* out;               /* attn_ring_fwd output shard */
+  const float* lse;              /* attn_ring_fwd LSE shard [batch, heads_q, seq_local] */
+  const void* d_out;             /* like out */
+  void* dq; void* dk; void* dv;  /* like q, k, v */
+  float softmax_scale;
+  int32_t has_band;
+  int64_t band_lo, band_hi;
+  const float* alibi_slopes;
+  int32_t zigzag;
+  void* workspace; size_t workspace_bytes;
+} attn_ring_bwd_params_t;
+
+size_t attn_ring_bwd_workspace_size(const attn_ring_bwd_params_t* p, int32_t world);
+int attn_ring_bwd(const attn_ring_bwd_params_t* p, attn_comm_t comm, void* compute_stream, void* comm_stream);
+
 /* ---- rotary position embedding ------------------------------------------- */
 /* Split-half RoPE on x (batch, heads, seq, head_dim), head_dim even and unit
  * stride:  out[..., i] = x1 cos - x2 sin,  out[..., i + half] = x1 sin + x2 cos

@@ -50,7 +50,8 @@ def test_ctypes_layout_matches_c_compiler(tmp_path):
         pytest.skip("gcc not available")
     structs = {"attn_mask_t": _lib.AttnMask, "attn_fwd_params_t": _lib.FwdParams,
                "attn_bwd_params_t": _lib.BwdParams, "attn_paged_params_t": _lib.PagedParams,
-               "attn_rope_params_t": _lib.RopeParams}
+               "attn_rope_params_t": _lib.RopeParams, "attn_ring_params_t": _lib.RingParams,
+               "attn_ring_bwd_params_t": _lib.RingBwdParams}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{ROOT}/include/attnb200.h"',
              "int main(void) {"]
     for cname, py in structs.items():
@@ -83,3 +84,29 @@ def test_block_table_entries_are_read_like_jax_indexing():
                         (-(2**31), 0)]:
         assert page(entry, nb) == want, entry
     assert page(3, 0) == -1
+
+
+def test_ring_communicator_entry_points_validate_and_fail_cleanly():
+    """attn_comm_*: a unique id is 128 opaque bytes made without a GPU; bad
+    arguments are ATTN_ERR_INVALID; without a GPU, init reports an error and
+    hands back no communicator (the GPU path runs in tests/test_ring_gpu.py)."""
+    import torch
+
+    if not pathlib.Path(_lib.LIB_PATH).exists():
+        pytest.fail("libattnb200.so is not built; run __graft_entry__.build()")
+    lib = _lib.load()
+    raw = (ctypes.c_char * _lib.COMM_ID_BYTES)()
+    rc = lib.attn_comm_unique_id(raw, _lib.COMM_ID_BYTES)
+    if rc == _lib.ATTN_ERR_NCCL:
+        pytest.skip("NCCL is not installed on this host")
+    assert rc == _lib.ATTN_OK and any(raw.raw)
+    assert lib.attn_comm_unique_id(raw, 16) == _lib.ATTN_ERR_INVALID
+    c = ctypes.c_void_p()
+    assert lib.attn_comm_init(ctypes.byref(c), 2, 5, raw, _lib.COMM_ID_BYTES) == _lib.ATTN_ERR_INVALID
+    assert lib.attn_comm_init(ctypes.byref(c), 1, 0, raw, 8) == _lib.ATTN_ERR_INVALID
+    assert lib.attn_comm_destroy(None) == _lib.ATTN_ERR_INVALID
+    if not torch.cuda.is_available():
+        assert lib.attn_comm_init(ctypes.byref(c), 1, 0, raw, _lib.COMM_ID_BYTES) != _lib.ATTN_OK
+        assert c.value is None
+    p = _lib.RingParams()
+    assert lib.attn_ring_fwd(ctypes.byref(p), None, None, None) == _lib.ATTN_ERR_INVALID
