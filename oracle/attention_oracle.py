@@ -31,7 +31,7 @@ __all__ = [
     "allocate_blocks", "append_kv", "gather_kv", "paged_attention",
     "paged_attention_batched", "softmax_scale", "bf16_round", "KVLayerCache",
     "init_kv_layer_cache", "update_kv_layer_cache", "kv_cache_attention", "rope_inv_freq",
-    "rope_cos_sin_table", "rope_cos_sin_from_positions", "apply_rope",
+    "rope_cos_sin_table", "rope_cos_sin_from_positions", "apply_rope", "mha_attention_core",
 ]
 
 
@@ -765,22 +765,97 @@ def kv_cache_attention(query, cache, *, mask=None, score_mod=None):
     return gqa_attention(query, cache.keys[:, :, :n], cache.values[:, :, :n], mask=mask, score_mod=score_mod)
 
 
+def mha_attention_core(query, key, value, *, num_heads, num_kv_heads, use_rope=False, rope_base=10000.0,
+                       rope_max_positions=4096, position_ids_q=None, position_ids_kv=None, kv_cache=None,
+                       attention_window=None, self_attention=True, mask=None, score_mod=None,
+                       base_score_mod=None, activation_dtype=None, rope_tables=None):
+    """``MultiHeadAttention.__call__`` between the projections (attnax/attention.py:340-445):
+    head split and transpose, RoPE of Q and K with table rows gathered at the
+    positions (``arange(seq)`` by default), the KV-cache concatenation and
+    update, the KV-head repeat (:395-407), the boolean sliding-window mask with
+    query positions shifted by the cached length (:417-431), and
+    ``standard_attention`` with the layer's mod composed before the call's.
+    ``query (B, Sq, Hq*D)``, ``key``/``value (B, Skv, Hkv*D)``; returns the
+    ``(B, Sq, Hq*D)`` result (and the updated cache when one is given).
+
+    ``activation_dtype`` is the dtype the layer runs in (default: the inputs'):
+    the reference builds its RoPE tables with ``out_dtype=query.dtype``
+    (attention.py:356-363), so a bf16 layer gets bf16-rounded positions and
+    frequencies, and its rotated q/k are bf16 values; ``"bfloat16"`` emulates
+    that on float32 inputs holding bf16 values.  ``rope_tables=(cos, sin)``
+    gives the ``(rope_max_positions, head_dim // 2)`` tables directly (a bf16
+    table depends on how ``pow`` rounds, which differs by one bf16 ulp between
+    libraries in a few entries; the tables are checked on their own)."""
+    b, sq, fq = query.shape
+    act = query.dtype if activation_dtype is None else activation_dtype
+    _, act_round = _rounder(act)
+    d = fq // num_heads
+    skv = key.shape[1]
+    q = query.reshape(b, sq, num_heads, d).transpose(0, 2, 1, 3)
+    k = key.reshape(b, skv, num_kv_heads, d).transpose(0, 2, 1, 3)
+    v = value.reshape(b, skv, num_kv_heads, d).transpose(0, 2, 1, 3)
+    if use_rope:
+        pq = np.broadcast_to(np.arange(sq)[None], (b, sq)) if position_ids_q is None else position_ids_q
+        pk = np.broadcast_to(np.arange(skv)[None], (b, skv)) if position_ids_kv is None else position_ids_kv
+        if rope_tables is None:
+            cos_t, sin_t = rope_cos_sin_table(rope_max_positions, d, rope_base, act)
+        else:
+            cos_t, sin_t = (np.asarray(t, dtype=np.float32) for t in rope_tables)
+        pq, pk = np.asarray(pq), np.asarray(pk)
+        q = act_round(apply_rope(q, cos_t[pq][:, None], sin_t[pq][:, None]))
+        k = act_round(apply_rope(k, cos_t[pk][:, None], sin_t[pk][:, None]))
+    new_cache = None
+    if kv_cache is not None:
+        past = int(kv_cache.length)
+        kc = np.concatenate([kv_cache.keys[:, :, :past], k], axis=2)
+        vc = np.concatenate([kv_cache.values[:, :, :past], v], axis=2)
+        new_cache = update_kv_layer_cache(kv_cache, k, v, past)
+        k, v = kc, vc
+    k, v = repeat_kv(k, num_heads), repeat_kv(v, num_heads)
+    if attention_window is not None and self_attention:
+        seq_kv_eff = k.shape[2]
+        if kv_cache is None:
+            win = make_sliding_window_mask(sq, seq_kv_eff, window_size=attention_window, causal=True)
+        else:
+            past = int(kv_cache.length)
+            qi = np.arange(sq) + past
+            ki = np.arange(seq_kv_eff)
+            win = ((ki[None, :] <= qi[:, None]) & (qi[:, None] - ki[None, :] < attention_window))[None, None]
+        mask = win if mask is None else (mask & win)
+    out = standard_attention(q, k, v, mask=mask, score_mod=compose_score_mods(base_score_mod, score_mod))
+    out = out.transpose(0, 2, 1, 3).reshape(b, sq, fq)
+    return (out, new_cache) if kv_cache is not None else out
+
+
 # ----------------------------------------------------------------------------
 # embeddings.py: rotary position embedding (RoPE)
 # ----------------------------------------------------------------------------
 
+def _rounder(dtype):
+    """Rounding after each op in ``dtype``; ``"bfloat16"`` (which numpy lacks)
+    computes in float32 and rounds every result to bf16, as JAX's bf16 ops do."""
+    if isinstance(dtype, str) and dtype == "bfloat16":
+        return np.float32, bf16_round
+    return dtype, lambda x: np.asarray(x).astype(dtype)
+
+
 def rope_inv_freq(head_dim, base, dtype=np.float32):
     """``base ** (-2i / head_dim)`` computed in ``dtype`` (embeddings.py:86-100)."""
     half = head_dim // 2
-    return (1.0 / (base ** (np.arange(0, half, dtype=dtype) / half))).astype(dtype)
+    dt, r = _rounder(dtype)
+    ar = r(np.arange(0, half, dtype=dt))
+    return r(1.0 / r(base ** r(ar / half)))
 
 
 def rope_cos_sin_table(max_seq_len, head_dim, base, dtype=np.float32):
     """cos/sin of ``position * inv_freq`` with positions and products in
-    ``dtype`` (embeddings.py:103-123): ``(max_seq_len, head_dim // 2)`` each."""
+    ``dtype`` (embeddings.py:103-123): ``(max_seq_len, head_dim // 2)`` each.
+    ``dtype="bfloat16"`` rounds positions, frequencies and their products to
+    bf16 as the reference does for a bf16 model."""
+    dt, r = _rounder(dtype)
     inv = rope_inv_freq(head_dim, base, dtype)
-    freqs = np.outer(np.arange(max_seq_len, dtype=dtype), inv).astype(dtype)
-    return np.cos(freqs).astype(dtype), np.sin(freqs).astype(dtype)
+    freqs = r(np.outer(r(np.arange(max_seq_len, dtype=dt)), inv))
+    return r(np.cos(freqs)), r(np.sin(freqs))
 
 
 def rope_cos_sin_from_positions(position_ids, head_dim, base, table_len, dtype=np.float32):
