@@ -38,9 +38,6 @@ constexpr int kThreads = 384;      // 3 warpgroups: softmax A, softmax B, TMA + 
 constexpr int kLaunchRegs = 168, kProducerRegs = 104, kSoftmaxRegs = 200;
 static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs == kThreads * kLaunchRegs, "register split");
 constexpr float kRescaleThreshold = 8.f;  // log2 units
-#ifndef ATTN_FWD2_REG_PARTIAL
-#define ATTN_FWD2_REG_PARTIAL 0  // band/prefix boundary tiles masked in registers (else via TMEM chunks)
-#endif
 #ifndef ATTN_FWD2_MAX3
 #define ATTN_FWD2_MAX3 0  // three-input max in the row-max tree
 #endif
@@ -63,7 +60,9 @@ struct Cfg {
   static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
   static constexpr int NBAR = 1 + 3 * STAGES + 6;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NBAR * 8;
-  static constexpr int SMEM = OFF_TMEMPTR + 16 + 1024;
+  // Document ids of a boundary kv tile, one 128-entry copy per softmax warp.
+  static constexpr int OFF_DOC = (OFF_TMEMPTR + 16 + 15) & ~15;
+  static constexpr int SMEM = OFF_DOC + 8 * BN * 4 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   __host__ __device__ static constexpr uint32_t s_col(int x) { return x ? 128u : 0u; }
   __host__ __device__ static constexpr uint32_t o_col(int x) { return x ? 256u + D : 256u; }
@@ -100,6 +99,13 @@ __device__ __forceinline__ float exp2_poly(float x) {
   const float f = x - (y - 12582912.f);
   const float p = fmaf(fmaf(fmaf(0.05517084f, f, 0.24260935f), f, 0.69326097f), f, 0.99992818f);
   return __int_as_float(__float_as_int(p) + ((__float_as_int(y) - 0x4B400000) << 23));
+}
+
+// Bits e (0..31) of a 32-column chunk with lo <= e <= hi.
+__device__ __forceinline__ uint32_t bit_range(long long lo, long long hi) {
+  if (hi < 0 || lo > 31 || hi < lo) return 0u;
+  const int l = lo < 0 ? 0 : (int)lo, h = hi > 31 ? 31 : (int)hi;
+  return (0xffffffffu >> (31 - h)) & (0xffffffffu << l);
 }
 
 // ACC: the ring variant that merges into a running result (Args::acc_o); a
@@ -309,23 +315,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and ALiBi is linear in the column: t = s*sl2 + slope*(c - d0).
     const bool linear_alibi = has_alibi && a.mask.has_band && a.mask.band_lo >= 0;
     const long long qg_row = a.mask.q_offset + my_q0 + r;
-    // Bias, boolean and document masks need per-column loads: their boundary
-    // tiles go through TMEM in 32-column chunks.  Band/prefix boundaries are
-    // masked in registers.
-    const bool complex_mask = !ATTN_FWD2_REG_PARTIAL || a.mask.bias || a.mask.bool_mask || a.mask.doc_q;
-    const int band_lo = a.mask.has_band ? clamp_i32(a.mask.band_lo) : -(1 << 30);
-    const int band_hi = a.mask.has_band ? clamp_i32(a.mask.band_hi) : (1 << 30);
-    const long long pref = a.mask.prefix_len ? (long long)a.mask.prefix_len[b] : -1;
+    // Bias and boolean masks need per-element loads: their boundary tiles are
+    // transformed in TMEM in 32-column chunks (mode 0 below).  Band, prefix
+    // and document boundaries are a keep-bit pass instead: a rolled loop over
+    // the four chunks sets dropped columns to -inf in TMEM, and the tile then
+    // takes the same unrolled code as a full tile.  A row that keeps nothing
+    // anywhere still ends with m_run == -FLT_MAX (LSE -inf, fixed up by
+    // fix_masked_rows_fwd_kernel), as with -FLT_MAX scores.
+    // (Mask parameters are read from the kernel arguments where they are used:
+    // only the two per-row values below stay in registers.)
+    const bool complex_mask = a.mask.bias || a.mask.bool_mask;
+    const bool has_doc = a.mask.doc_q != nullptr;
+    const int pref = a.mask.prefix_len ? a.mask.prefix_len[b] : 0;
+    const int doc_row = (has_doc && my_act && my_q0 + r < a.Sq)
+                            ? a.mask.doc_q[(long long)b * a.mask.doc_q_bstride + a.mask.q_offset + my_q0 + r]
+                            : 0;
+    int* doc_ids = reinterpret_cast<int*>(sp + C::OFF_DOC) + warp * BN;  // this warp's copy
     for (int t = 0; t < n_tiles; ++t) {
       const int j = kv_tile(t);
       const int st = state_at(my_act, my_jl, my_jh, my_q0, my_q1, j);
       if (st == kSkip) continue;
+      const int k0 = j * BN;
+      const bool part = st == kPartial;
+      // Document ids of a boundary tile's columns: loaded before the wait so
+      // the latency hides behind the S MMA.
+      int cid[BN / 32];
+      if (part && has_doc && !complex_mask) {
+        const int32_t* doc_cols = a.mask.doc_kv + (long long)b * a.mask.doc_kv_bstride + a.mask.kv_offset;
+#pragma unroll
+        for (int u = 0; u < BN / 32; ++u) {
+          const int kc = k0 + u * 32 + lane;
+          cid[u] = kc < a.Skv ? doc_cols[kc] : 0;
+        }
+      }
       ok = __all_sync(0xffffffffu, mbar_wait(s_full(x), i & 1, kStatusTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-      const int k0 = j * BN;
       const uint32_t s_addr = tmem + lane_base + C::s_col(x);
-      if (st == kPartial && complex_mask) {
+      if (part && !complex_mask) {
+        if (has_doc) {
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < BN / 32; ++u) doc_ids[u * 32 + lane] = cid[u];
+          __syncwarp();
+        }
+        // q - kv of this row at column 0 of the tile (global positions)
+        const long long dq0 = qg_row - (a.mask.kv_offset + k0);
+        const long long kv0 = a.mask.kv_offset + k0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(s_addr + c * 32, raw);
+          const long long dc = dq0 - c * 32;  // q - kv at chunk column e is dc - e
+          uint32_t keep = bit_range(0, (long long)a.Skv - k0 - c * 32 - 1);  // inside the sequence
+          if (a.mask.has_band) keep &= bit_range(dc - a.mask.band_hi, dc - a.mask.band_lo);
+          if (a.mask.prefix_len) keep &= bit_range(0, pref - (kv0 + c * 32) - 1) | bit_range(0, dc);
+          if (has_doc) {
+            const int4* ids = reinterpret_cast<const int4*>(doc_ids + c * 32);
+            uint32_t same = 0u;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int4 v = ids[u];
+              same |= ((uint32_t)(v.x == doc_row) | ((uint32_t)(v.y == doc_row) << 1) |
+                       ((uint32_t)(v.z == doc_row) << 2) | ((uint32_t)(v.w == doc_row) << 3))
+                      << (4 * u);
+            }
+            keep &= same;
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (!((keep >> e) & 1u)) raw[e] = 0xff800000u;  // -inf
+          tmem_st32(s_addr + c * 32, raw);
+        }
+        tmem_wait_st();
+      } else if (part) {
         // Boundary tile: mask/transform 32 columns at a time in TMEM so the
         // per-column mask state never competes with the 128 scores.
 #pragma unroll 1
@@ -350,17 +414,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       float mxp[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mxp[e] = -FLT_MAX;
-      // Mode: 0 = already transformed (complex boundary), 1 = plain scale (full
-      // tile, scale folded into exp2), 2 = linear ALiBi, 3 = general ALiBi,
-      // 4 = plain scale applied before masking (band/prefix boundary).
-      const bool part = st == kPartial;
-      const int mode = (part && complex_mask) ? 0
-                       : (!has_alibi ? (part ? 4 : 1) : (linear_alibi ? 2 : 3));
+      // Mode: 0 = already transformed (bias/boolean boundary), 1 = plain scale
+      // (scale folded into exp2), 2 = linear ALiBi, 3 = general ALiBi.  Dropped
+      // columns of band/prefix/document boundary tiles are -inf already.
+      const int mode = (part && complex_mask) ? 0 : (!has_alibi ? 1 : (linear_alibi ? 2 : 3));
       const int d0 = clamp_i32(qg_row - (a.mask.kv_offset + k0));
       const float fd0 = (float)d0;
       const float base = -slope_l2 * fd0;
-      const int ncols = min(BN, a.Skv - k0);
-      const int pref_cols = (int)ll_max(-1, ll_min((long long)BN, pref - (a.mask.kv_offset + k0)));
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
 #pragma unroll
@@ -394,24 +454,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (mode == 3) {
 #pragma unroll
           for (int c = h * 64; c < h * 64 + 64; ++c) s[c] = fmaf(-slope_l2, fabsf(fd0 - (float)c), s[c] * a.sl2);
-        } else if (mode == 4) {
-          const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2), z = f2_pack(0.f, 0.f);
-#pragma unroll
-          for (int c = h * 64; c < h * 64 + 64; c += 2) {
-            float lo, hi;
-            f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, z), lo, hi);
-            s[c] = lo;
-            s[c + 1] = hi;
-          }
-        }
-        if (part && !complex_mask) {
-          // keep iff band_lo <= q - kv <= band_hi and (kv < prefix or kv <= q); pad columns are -inf
-#pragma unroll
-          for (int c = h * 64; c < h * 64 + 64; ++c) {
-            const int d = d0 - c;
-            const bool keep = d >= band_lo && d <= band_hi && (c < pref_cols || d >= 0 || pref < 0);
-            s[c] = c < ncols ? (keep ? s[c] : -FLT_MAX) : -INFINITY;
-          }
         }
 #if ATTN_FWD2_MAX3
 #pragma unroll

@@ -159,6 +159,42 @@ def test_lse_matches_oracle():
     assert np.max(np.abs(npy(lse) - want)) < 1e-3
 
 
+@pytest.mark.parametrize("mod", ["causal", "window", "causal_alibi", "prefix", "document_causal"])
+@pytest.mark.parametrize("D", [64, 128])
+def test_forward_at_offsets_boundary_tiles(mod, D):
+    """Band, prefix and document boundary tiles at global offsets, the calls a
+    ring hop makes: queries start before the keys, so the first rows keep no
+    key under the causal chains.  Rows that keep a key match the oracle (out
+    and LSE); rows that keep none come back with LSE -inf (an empty partial)."""
+    from attnax_b200._spec import build_spec
+    from attnax_b200.flash import fwd_raw
+
+    rng = np.random.default_rng(12)
+    B, Hq, Hkv, Sq, Skv = 2, 4, 2, 300, 260
+    q0, k0 = 170, 333
+    total = max(q0 + Sq, k0 + Skv)
+    if mod == "prefix":
+        pref = np.array([400, 100], np.int32)  # batch 0: the prefix reaches into the keys; batch 1: causal only
+        m_ax, m_o = ax.prefix_lm_mod(pref), O.prefix_lm_mod(pref)
+    else:
+        m_ax, m_o = pair(mod, Hq, total, B)
+    q = randn(rng, (B, Hq, Sq, D), True)
+    k, v = (randn(rng, (B, Hkv, Skv, D), True) for _ in range(2))
+    spec = build_spec(m_ax, None, batch=B, heads_q=Hq, seq_q=Sq, seq_kv=Skv, device=torch.device(DEV),
+                      q_offset=q0, kv_offset=k0)
+    out, lse = fwd_raw(T(q), T(k), T(v), spec)
+    kr, vr = O.repeat_kv(k, Hq), O.repeat_kv(v, Hq)
+    want_o, want_l = O.standard_attention_lse(q, kr, vr, score_mod=m_o, q_offset=q0, kv_offset=k0)
+    s = O.attention_oracle._final_scores(q, kr, None, m_o, q0, k0)
+    empty = np.all(s == np.finfo(s.dtype).min, axis=-1)
+    got_o, got_l = npy(out), npy(lse)
+    assert np.all(np.isneginf(got_l[empty])), "rows that keep no key must return lse -inf"
+    keep = ~empty
+    assert keep.sum() > 0
+    assert_bf16_close(got_o[keep], want_o[keep], f"offsets {mod} D{D}")
+    assert np.max(np.abs(got_l[keep] - want_l[keep])) < 1e-3
+
+
 @pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.bfloat16, 64), (torch.float32, 64)])
 @pytest.mark.parametrize("mod", ["causal", "window_alibi", "document_causal"])
 def test_backward(dtype, D, mod):
