@@ -233,6 +233,14 @@ struct RowCtx {
   bool alibi, band, prefix, doc;
 };
 
+// Bits e (0..31) of a 32-column chunk with lo <= e <= hi (a keep mask of a
+// boundary tile's columns under a band or prefix rule).
+__device__ __forceinline__ uint32_t bit_range(long long lo, long long hi) {
+  if (hi < 0 || lo > 31 || hi < lo) return 0u;
+  const int l = lo < 0 ? 0 : (int)lo, h = hi > 31 ? 31 : (int)hi;
+  return (0xffffffffu >> (31 - h)) & (0xffffffffu << l);
+}
+
 __device__ __forceinline__ int clamp_i32(long long x) {
   return (int)(x < -(1ll << 30) ? -(1ll << 30) : (x > (1ll << 30) ? (1ll << 30) : x));
 }

@@ -399,6 +399,15 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
     const bool fast_mask = ATTN_BWD_FAST_FULL && (!a.mask.alibi_slopes || (a.mask.has_band && a.mask.band_lo >= 0));
     const long long kg_row = a.mask.kv_offset + k0 + r;
     const unsigned long long sl2x2 = f2_pack(a.sl2, a.sl2);
+    // Boundary tiles under band, prefix and document masks take the full-tile
+    // arithmetic as well; a keep mask of the thread's HC columns then zeroes P
+    // and dS of the dropped ones (a select, so scores the mask drops may
+    // overflow freely).  Bias and boolean masks keep the transform_row path.
+    const bool bits_mask = fast_mask && !a.mask.bias && !a.mask.bool_mask;
+    const bool has_doc = a.mask.doc_q != nullptr;
+    const int doc_row =
+        (has_doc && k0 + r < a.Skv) ? a.mask.doc_kv[(long long)b * a.mask.doc_kv_bstride + kg_row] : 0;
+    const bool row_in_prefix = a.mask.prefix_len && kg_row < (long long)a.mask.prefix_len[b];
     int i = 0;
     bool ok = true;
     if (C::V_TMEM) {
@@ -497,6 +506,14 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
       if (st == kSkip) continue;
       const int hq = hkv * a.group + g, q0 = qt * QT;
       const int s = i % ST;
+      const bool part_bits = st == kPartial && bits_mask;
+      int cid = 0;  // document id of q column lane of this thread's half (loaded before the wait)
+      if (part_bits && has_doc) {
+        const int qc = q0 + half * HC + lane;
+        cid = (lane < HC && qc < a.Sq)
+                  ? a.mask.doc_q[(long long)b * a.mask.doc_q_bstride + a.mask.q_offset + qc]
+                  : 0;
+      }
       ok = ok && __all_sync(0xffffffffu, mbar_wait(s_full(i % NSB), (i / NSB) & 1, kStatusTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
@@ -509,9 +526,10 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
       const int c0 = q0 + half * HC;
       const float* sl = reinterpret_cast<const float*>(sp + C::OFF_ST + s * C::STAGE + 2 * C::QD_BYTES) + half * HC;
       const float* sd = sl + QT;
-      if (st == kFull && fast_mask) {
+      if ((st == kFull && fast_mask) || part_bits) {
         // (a full tile has all KROWS kv rows inside the sequence; q columns
-        // past the end carry lse2 = +inf and delta = 0, so P = dS = 0 there)
+        // past the end carry lse2 = +inf and delta = 0, so P = dS = 0 there;
+        // a boundary tile's keep mask covers both)
         static_assert(HC <= 32, "one column term per lane");
         const float slope = a.mask.alibi_slopes ? __ldg(a.mask.alibi_slopes + hq) * kLog2e : 0.f;
         __syncwarp();
@@ -533,6 +551,24 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
                                                             e ? f2_pack(d4.z, d4.w) : f2_pack(d4.x, d4.y)));
             f2_unpack(p2, sc[c + e], sc[c + e + 1]);
             f2_unpack(g2, dp[c + e], dp[c + e + 1]);
+          }
+        }
+        if (part_bits) {
+          const long long dd = a.mask.q_offset + c0 - kg_row;  // q - kv at this thread's column 0
+          uint32_t keep = k0 + r < a.Skv ? bit_range(0, (long long)a.Sq - c0 - 1) : 0u;
+          if (a.mask.has_band) keep &= bit_range(a.mask.band_lo - dd, a.mask.band_hi - dd);
+          if (a.mask.prefix_len && !row_in_prefix) keep &= bit_range(-dd, 31);  // kv < prefix, else kv <= q
+          if (has_doc) {
+            uint32_t same = 0u;
+#pragma unroll
+            for (int e = 0; e < HC; ++e) same |= (uint32_t)(__shfl_sync(0xffffffffu, cid, e) == doc_row) << e;
+            keep &= same;
+          }
+#pragma unroll
+          for (int c = 0; c < HC; ++c) {
+            const bool k = (keep >> c) & 1u;
+            sc[c] = k ? sc[c] : 0.f;
+            dp[c] = k ? dp[c] : 0.f;
           }
         }
       } else {

@@ -101,13 +101,6 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return __int_as_float(__float_as_int(p) + ((__float_as_int(y) - 0x4B400000) << 23));
 }
 
-// Bits e (0..31) of a 32-column chunk with lo <= e <= hi.
-__device__ __forceinline__ uint32_t bit_range(long long lo, long long hi) {
-  if (hi < 0 || lo > 31 || hi < lo) return 0u;
-  const int l = lo < 0 ? 0 : (int)lo, h = hi > 31 ? 31 : (int)hi;
-  return (0xffffffffu >> (31 - h)) & (0xffffffffu << l);
-}
-
 // ACC: the ring variant that merges into a running result (Args::acc_o); a
 // separate instantiation so the plain forward's epilogue stays as it is.
 template <int D, bool BF16, bool ACC = false>

@@ -195,6 +195,45 @@ def test_forward_at_offsets_boundary_tiles(mod, D):
     assert np.max(np.abs(got_l[keep] - want_l[keep])) < 1e-3
 
 
+@pytest.mark.parametrize("mod", ["causal", "window", "causal_alibi", "prefix", "document_causal"])
+@pytest.mark.parametrize("D", [64, 128])
+def test_backward_at_offsets_boundary_tiles(mod, D):
+    """Backward through band, prefix and document boundary tiles at global
+    offsets (queries after the start of the keys, so every row keeps a key):
+    the gradients of the attention whose mods see positions shifted by the
+    offsets."""
+    from attnax_b200._spec import build_spec
+    from attnax_b200.flash import bwd_raw, fwd_raw
+
+    rng = np.random.default_rng(13)
+    B, Hq, Hkv, Sq, Skv = 2, 4, 2, 300, 260
+    q0, k0 = 400, 333
+    total = max(q0 + Sq, k0 + Skv)
+    if mod == "prefix":
+        pref = np.array([400, 100], np.int32)
+        m_ax, m_o = ax.prefix_lm_mod(pref), O.prefix_lm_mod(pref)
+    elif mod == "window":
+        m_ax, m_o = ax.sliding_window_mod(150), O.sliding_window_mod(150)
+    else:
+        m_ax, m_o = pair(mod, Hq, total, B)
+
+    def shifted(scores, b_idx, h_idx, q_idx, kv_idx):
+        return m_o(scores, b_idx, h_idx, q_idx + q0, kv_idx + k0)
+
+    q = randn(rng, (B, Hq, Sq, D), True)
+    k, v = (randn(rng, (B, Hkv, Skv, D), True) for _ in range(2))
+    do = randn(rng, (B, Hq, Sq, D), True)
+    spec = build_spec(m_ax, None, batch=B, heads_q=Hq, seq_q=Sq, seq_kv=Skv, device=torch.device(DEV),
+                      q_offset=q0, kv_offset=k0)
+    tq, tk, tv = T(q), T(k), T(v)
+    out, lse = fwd_raw(tq, tk, tv, spec)
+    assert np.all(np.isfinite(npy(lse))), "every row keeps a key at these offsets"
+    got = bwd_raw(tq, tk, tv, out, lse, T(do), spec)
+    want = O.gqa_attention_bwd(q, k, v, do, score_mod=shifted)
+    for name, g, w in zip(("dq", "dk", "dv"), got, want):
+        assert_bf16_grad_close(npy(g), w, f"offsets {mod} D{D} {name}")
+
+
 @pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.bfloat16, 64), (torch.float32, 64)])
 @pytest.mark.parametrize("mod", ["causal", "window_alibi", "document_causal"])
 def test_backward(dtype, D, mod):
