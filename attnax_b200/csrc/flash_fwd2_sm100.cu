@@ -265,17 +265,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool ax = kept(0, j), bx = kept(1, j);
         if (!ax && !bx) continue;
         const int s = n % S;
+        // PV_A of the previous kv tile needs only that tile's V: it is issued
+        // before waiting for this tile's K, so a late K cannot hold it up.
+        if (prev_s >= 0) {
+          ok = mbar_wait(v_full(prev_s), ((n - 1) / S) & 1, kStatusTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          if (prev_act[0]) ok = issue_pv(0, prev_s);
+          if (!ok) break;
+        }
         ok = mbar_wait(k_full(s), (n / S) & 1, kStatusTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        if (prev_s >= 0) ok = mbar_wait(v_full(prev_s), ((n - 1) / S) & 1, kStatusTimeoutMma);
+        if (ax) issue_s(0, s);
+        if (prev_act[1]) ok = issue_pv(1, prev_s);
         if (!ok) break;
-        if (prev_act[0]) ok = issue_pv(0, prev_s);
-        if (ok && ax) issue_s(0, s);
-        if (ok && prev_act[1]) ok = issue_pv(1, prev_s);
-        if (ok && bx) issue_s(1, s);
-        if (!ok) break;
+        // PV_B was the previous stage's last reader: release the stage now
+        // (the commit tracks every MMA issued so far), not after S_B, so the
+        // next K/V load into it starts one GEMM earlier.
         if (prev_s >= 0) umma_commit(kv_empty(prev_s));
+        if (bx) issue_s(1, s);
         prev_s = s;
         prev_act[0] = ax;
         prev_act[1] = bx;
