@@ -178,6 +178,37 @@ __global__ void doc_cross_range_kernel(const int2* row_tiles, int n_row, const i
   if (lane == 0) out[(long long)b * n_row + t] = hi < 0 ? make_int2(0, 0) : make_int2(lo, hi + 1);
 }
 
+// Launch order of the forward's two-query-tile CTAs under a document mask.
+// Per batch, CTA indices are ranked by their kv-tile count (the document
+// range of q_jr intersected with the band, summed over the CTA's two query
+// tiles of bm == kDocTile rows), largest first, later tiles first on ties,
+// so the longest CTAs start in the first wave.  One block per batch;
+// n_ctas ints of dynamic shared memory.
+__global__ void doc_cta_order_kernel(attn_mask_t m, const int2* q_jr, int nq_doc, int seq_q, int seq_kv, int bm,
+                                     int bn, int n_ctas, int* order) {
+  extern __shared__ int work[];
+  const int b = blockIdx.x;
+  for (int c = threadIdx.x; c < n_ctas; c += blockDim.x) {
+    int tot = 0;
+    for (int x = 0; x < 2; ++x) {
+      const int q0 = c * 2 * bm + x * bm;
+      if (q0 >= seq_q) continue;
+      int lo, hi;
+      band_tile_range(m, q0, min(q0 + bm, seq_q), seq_kv, bn, &lo, &hi);
+      const int2 r = q_jr[(long long)b * nq_doc + q0 / kDocTile];
+      tot += max(0, min(hi, r.y) - max(lo, r.x));
+    }
+    work[c] = tot;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < n_ctas; c += blockDim.x) {
+    const int wc = work[c];
+    int rank = 0;
+    for (int o = 0; o < n_ctas; ++o) rank += (work[o] > wc) || (work[o] == wc && o > c);
+    order[(long long)b * n_ctas + rank] = c;
+  }
+}
+
 // (min, max) of document ids over kDocTile-row tiles of global positions
 // offset + [t*kDocTile, min((t+1)*kDocTile, len)).
 __global__ void doc_tile_range_kernel(const int32_t* ids, long long bstride, long long offset,

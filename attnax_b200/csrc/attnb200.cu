@@ -168,8 +168,16 @@ static int launch_doc_ranges(const attn_mask_t& m, int batch, int seq_q, int seq
 }
 
 struct FwdWorkspace {
-  size_t doc_q = 0, doc_kv = 0, doc_jr = 0, lse = 0, total = 0;
+  size_t doc_q = 0, doc_kv = 0, doc_jr = 0, doc_order = 0, lse = 0, total = 0;
 };
+
+// Document masks: the two-tile forward runs its CTAs longest first
+// (doc_cta_order_kernel) when the per-batch ranking fits one block.
+constexpr int kMaxOrderedCtas = 4096;
+static int fwd2_ctas(int seq_q) { return (seq_q + 2 * fwd2::BM - 1) / (2 * fwd2::BM); }
+static bool doc_ordered(const attn_fwd_params_t* p) {
+  return p->mask.doc_q && p->seq_q > fwd::BM && fwd2_ctas(p->seq_q) <= kMaxOrderedCtas;
+}
 
 static FwdWorkspace fwd_workspace_layout(const attn_fwd_params_t* p) {
   FwdWorkspace w;
@@ -182,6 +190,10 @@ static FwdWorkspace fwd_workspace_layout(const attn_fwd_params_t* p) {
     off += align256((size_t)p->batch * nk * sizeof(int2));
     w.doc_jr = off;
     off += align256((size_t)p->batch * nq * sizeof(int2));
+    if (doc_ordered(p)) {
+      w.doc_order = off;
+      off += align256((size_t)p->batch * fwd2_ctas(p->seq_q) * sizeof(int));
+    }
   }
   if (p->fix_masked_rows && !p->lse) {
     w.lse = off;
@@ -225,7 +237,8 @@ struct RingAcc {
 
 template <int D, bool BF16>
 static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2* dq_t, const int2* dkv_t,
-                             const int2* djr, cudaStream_t st, const RingAcc* acc = nullptr) {
+                             const int2* djr, cudaStream_t st, const RingAcc* acc = nullptr,
+                             const int* order = nullptr) {
   CUtensorMap tq, tk, tv;
   if (!make_tmap(&tq, p->dtype, p->q, p->batch, p->num_heads_q, p->seq_q, D, p->q_strides, fwd2::BM) ||
       !make_tmap(&tk, p->dtype, p->k, p->batch, p->num_heads_kv, p->seq_kv, D, p->k_strides, fwd2::BN) ||
@@ -234,7 +247,7 @@ static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2*
   fwd2::Args a;
   a.B = p->batch; a.Hq = p->num_heads_q; a.Hkv = p->num_heads_kv; a.Sq = p->seq_q; a.Skv = p->seq_kv;
   a.group = p->num_heads_q / p->num_heads_kv;
-  a.n_ctas = (p->seq_q + 2 * fwd2::BM - 1) / (2 * fwd2::BM);
+  a.n_ctas = fwd2_ctas(p->seq_q);
   a.sl2 = p->softmax_scale * kLog2e;
   a.out = p->out;
   a.o_s0 = p->o_strides[0]; a.o_s1 = p->o_strides[1]; a.o_s2 = p->o_strides[2];
@@ -242,6 +255,7 @@ static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2*
   a.doc_q_tiles = dq_t; a.doc_kv_tiles = dkv_t; a.doc_jrange = djr;
   a.nq_doc = (p->seq_q + kDocTile - 1) / kDocTile;
   a.nk_doc = (p->seq_kv + kDocTile - 1) / kDocTile;
+  a.cta_order = order;
   a.acc_o = acc ? acc->o : nullptr;
   a.acc_lse = acc ? acc->lse : nullptr;
   a.acc_rows = acc ? acc->rows : 0;
@@ -261,16 +275,17 @@ static int launch_sm100_fwd2(const attn_fwd_params_t* p, float* lse, const int2*
       return ATTN_ERR_CUDA;
     attr_dev[acc ? 1 : 0] = dev;
   }
-  dim3 grid(a.n_ctas, p->num_heads_q, p->batch);
+  // With an order table, blockIdx.x walks (rank, head) with heads fastest.
+  dim3 grid = order ? dim3(a.n_ctas * p->num_heads_q, 1, p->batch) : dim3(a.n_ctas, p->num_heads_q, p->batch);
   kern<<<grid, fwd2::kThreads, smem, st>>>(tq, tk, tv, a);
   return launch_status();
 }
 
 template <int D, bool BF16>
 static int launch_sm100_fwd(const attn_fwd_params_t* p, float* lse, const int2* dq_t, const int2* dkv_t,
-                            const int2* djr, cudaStream_t st) {
+                            const int2* djr, cudaStream_t st, const int* order = nullptr) {
   if (p->seq_q > fwd::BM) {
-    const int rc = launch_sm100_fwd2<D, BF16>(p, lse, dq_t, dkv_t, djr, st);
+    const int rc = launch_sm100_fwd2<D, BF16>(p, lse, dq_t, dkv_t, djr, st, nullptr, order);
     if (rc != ATTN_ERR_UNSUPPORTED) return rc;
   }
   CUtensorMap tq, tk, tv;
@@ -377,22 +392,31 @@ int attn_fwd(const attn_fwd_params_t* p, void* stream) {
   const bool tc = tc_layout_ok(p);
   if (!tc && !simt_dim_ok(p->head_dim)) return ATTN_ERR_UNSUPPORTED;
   int2 *dq_t = nullptr, *dkv_t = nullptr, *djr = nullptr;
+  int* order = nullptr;
   if (p->mask.doc_q && tc) {
     dq_t = reinterpret_cast<int2*>(ws + w.doc_q);
     dkv_t = reinterpret_cast<int2*>(ws + w.doc_kv);
     djr = reinterpret_cast<int2*>(ws + w.doc_jr);
     const int lrc = launch_doc_ranges(p->mask, p->batch, p->seq_q, p->seq_kv, dq_t, dkv_t, djr, nullptr, st);
     if (lrc != ATTN_OK) return lrc;
+    if (doc_ordered(p)) {
+      order = reinterpret_cast<int*>(ws + w.doc_order);
+      const int nc = fwd2_ctas(p->seq_q);
+      doc_cta_order_kernel<<<p->batch, 256, nc * sizeof(int), st>>>(
+          p->mask, djr, (p->seq_q + kDocTile - 1) / kDocTile, p->seq_q, p->seq_kv, fwd2::BM, fwd2::BN, nc, order);
+      const int orc = launch_status();
+      if (orc != ATTN_OK) return orc;
+    }
   }
   int rc;
   if (tc) {
     const bool bf = p->dtype == ATTN_BF16;
     if (p->head_dim == 128)
-      rc = bf ? launch_sm100_fwd<128, true>(p, lse, dq_t, dkv_t, djr, st)
-              : launch_sm100_fwd<128, false>(p, lse, dq_t, dkv_t, djr, st);
+      rc = bf ? launch_sm100_fwd<128, true>(p, lse, dq_t, dkv_t, djr, st, order)
+              : launch_sm100_fwd<128, false>(p, lse, dq_t, dkv_t, djr, st, order);
     else
-      rc = bf ? launch_sm100_fwd<64, true>(p, lse, dq_t, dkv_t, djr, st)
-              : launch_sm100_fwd<64, false>(p, lse, dq_t, dkv_t, djr, st);
+      rc = bf ? launch_sm100_fwd<64, true>(p, lse, dq_t, dkv_t, djr, st, order)
+              : launch_sm100_fwd<64, false>(p, lse, dq_t, dkv_t, djr, st, order);
   } else if (p->dtype == ATTN_F32) {
     rc = launch_simt_fwd<float>(p, lse, st);
   } else if (p->dtype == ATTN_BF16) {
@@ -439,8 +463,16 @@ static int bwd_seq_pad(const attn_bwd_params_t* p) { return (p->seq_q + 127) / 1
 static bool bwd_fused_dq(const attn_bwd_params_t* p) { return ATTN_BWD_FUSED_DQ && p->head_dim == 128; }
 
 struct BwdWorkspace {
-  size_t lse2 = 0, dq_acc = 0, doc_q = 0, doc_kv = 0, doc_q_jr = 0, doc_kv_qr = 0, total = 0;  // delta at 0
+  size_t lse2 = 0, dq_acc = 0, doc_q = 0, doc_kv = 0, doc_q_jr = 0, doc_kv_qr = 0, doc_kv_order = 0,
+         total = 0;  // delta at 0
 };
+
+// Document masks: dkdv_kernel runs its kv tiles longest first (doc_kv_order_kernel)
+// when the per-batch ranking fits one block.
+static int bwd_kv_tiles(int seq_kv) { return (seq_kv + bwd::KROWS - 1) / bwd::KROWS; }
+static bool bwd_doc_ordered(const attn_bwd_params_t* p) {
+  return p->mask.doc_q && bwd_kv_tiles(p->seq_kv) <= kMaxOrderedCtas;
+}
 
 static BwdWorkspace bwd_workspace_layout(const attn_bwd_params_t* p) {
   BwdWorkspace w;
@@ -459,6 +491,10 @@ static BwdWorkspace bwd_workspace_layout(const attn_bwd_params_t* p) {
     off += align256(p->batch * nq * sizeof(int2));
     w.doc_kv_qr = off;
     off += align256(p->batch * nk * sizeof(int2));
+    if (bwd_doc_ordered(p)) {
+      w.doc_kv_order = off;
+      off += align256((size_t)p->batch * bwd_kv_tiles(p->seq_kv) * sizeof(int));
+    }
   }
   w.total = off;
   return w;
@@ -466,6 +502,7 @@ static BwdWorkspace bwd_workspace_layout(const attn_bwd_params_t* p) {
 
 struct BwdDocTables {
   const int2 *q_t = nullptr, *kv_t = nullptr, *q_jr = nullptr, *kv_qr = nullptr;
+  const int* kv_order = nullptr;
 };
 
 // Sets the kernel's dynamic shared-memory limit once per device.
@@ -506,6 +543,8 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
   a.doc_q_tiles = doc.q_t; a.doc_kv_tiles = doc.kv_t; a.doc_q_jr = doc.q_jr; a.doc_kv_qr = doc.kv_qr;
   a.nq_doc = (p->seq_q + kDocTile - 1) / kDocTile;
   a.nk_doc = (p->seq_kv + kDocTile - 1) / kDocTile;
+  a.kv_order = doc.kv_order;
+  a.n_kt = bwd_kv_tiles(p->seq_kv);
   CUtensorMap q64, do64, k128, v128, q128, do128, k64, v64;
   const int B = p->batch, Hq = p->num_heads_q, Hkv = p->num_heads_kv, Sq = p->seq_q, Skv = p->seq_kv;
   if (!make_tmap(&q64, p->dtype, p->q, B, Hq, Sq, D, p->q_strides, QT) ||
@@ -517,7 +556,8 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
       !make_tmap(&k64, p->dtype, p->k, B, Hkv, Skv, D, p->k_strides, KT) ||
       !make_tmap(&v64, p->dtype, p->v, B, Hkv, Skv, D, p->v_strides, KT))
     return ATTN_ERR_INVALID;
-  const dim3 grid_kv((Skv + KROWS - 1) / KROWS, Hkv, B);
+  // With an order table, blockIdx.x walks (rank, kv head) with heads fastest.
+  const dim3 grid_kv = a.kv_order ? dim3(a.n_kt * Hkv, 1, B) : dim3(a.n_kt, Hkv, B);
   if constexpr (D == 128) {
     if (bwd_fused_dq(p)) {
       // dQ accumulated in fp32 by the dK/dV kernel, then scaled and converted.
@@ -601,6 +641,15 @@ int attn_bwd(const attn_bwd_params_t* p, void* stream) {
       rc = launch_doc_ranges(p->mask, p->batch, p->seq_q, p->seq_kv, q_t, kv_t, q_jr, kv_qr, st);
       if (rc != ATTN_OK) return rc;
       doc.q_t = q_t; doc.kv_t = kv_t; doc.q_jr = q_jr; doc.kv_qr = kv_qr;
+      if (bwd_doc_ordered(p)) {
+        int* kv_order = reinterpret_cast<int*>(wb + wl.doc_kv_order);
+        const int nkt = bwd_kv_tiles(p->seq_kv);
+        bwd::doc_kv_order_kernel<<<p->batch, 256, nkt * sizeof(int), st>>>(
+            p->mask, kv_qr, (p->seq_kv + kDocTile - 1) / kDocTile, p->seq_q, p->seq_kv, nkt, kv_order);
+        rc = launch_status();
+        if (rc != ATTN_OK) return rc;
+        doc.kv_order = kv_order;
+      }
     }
     const bool bf = p->dtype == ATTN_BF16;
     if (p->head_dim == 128)

@@ -110,6 +110,10 @@ struct Args {
   const int2* doc_q_jr;
   const int2* doc_kv_qr;
   int nq_doc, nk_doc;
+  // Document masks: [B][n_kt] kv-tile indices of dkdv_kernel, longest first
+  // (or null); its grid is then (n_kt * Hkv, 1, B) with heads fastest.
+  const int* kv_order;
+  int n_kt;
 };
 
 // q-tile index range [lo, hi) (tiles of QT) that the band allows for kv rows [k0, k1).
@@ -129,6 +133,31 @@ __device__ __forceinline__ void band_q_range(const attn_mask_t& m, int k0, int k
     }
     *lo = (int)(r_lo / QT);
     *hi = (int)(r_hi / QT) + 1;
+  }
+}
+
+// Launch order of dkdv_kernel's kv tiles under a document mask: per batch, kv
+// tile indices ranked by the q tiles they visit (band range intersected with
+// the document range kv_qr), largest first (earlier tiles first on ties), so
+// the longest CTAs start in the first wave.  One block per batch; n_kt ints
+// of dynamic shared memory.
+static_assert(KROWS == kDocTile, "kv tiles of dkdv_kernel are the document tiles");
+__global__ void doc_kv_order_kernel(attn_mask_t m, const int2* kv_qr, int nk_doc, int Sq, int Skv, int n_kt,
+                                    int* order) {
+  extern __shared__ int work[];
+  const int b = blockIdx.x;
+  for (int t = threadIdx.x; t < n_kt; t += blockDim.x) {
+    int lo, hi;
+    band_q_range(m, t * KROWS, min((t + 1) * KROWS, Skv), Sq, &lo, &hi);
+    const int2 r = kv_qr[(long long)b * nk_doc + t];
+    work[t] = max(0, min(hi, r.y * (kDocTile / QT)) - max(lo, r.x * (kDocTile / QT)));
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < n_kt; t += blockDim.x) {
+    const int wt = work[t];
+    int rank = 0;
+    for (int o = 0; o < n_kt; ++o) rank += (work[o] > wt) || (work[o] == wt && o < t);
+    order[(long long)b * n_kt + rank] = t;
   }
 }
 
@@ -205,7 +234,16 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
   const uint32_t sb = (raw_base + 1023u) & ~1023u;
   uint8_t* sp = smem_raw + (sb - raw_base);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
+  const int b = blockIdx.z;
+  int kt, hkv;
+  if (a.kv_order) {
+    const int k = (int)blockIdx.x / a.Hkv;
+    hkv = (int)blockIdx.x - k * a.Hkv;
+    kt = a.kv_order[(long long)b * a.n_kt + k];
+  } else {
+    kt = blockIdx.x;  // early kv tiles carry the most q tiles under causal bands
+    hkv = blockIdx.y;
+  }
   const int k0 = kt * KROWS, k1 = min(k0 + KROWS, a.Skv);
 
   const uint32_t bar0 = sb + C::OFF_BAR;

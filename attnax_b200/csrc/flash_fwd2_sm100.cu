@@ -79,6 +79,9 @@ struct Args {
   const int2* doc_kv_tiles;
   const int2* doc_jrange;  // per q tile: kv tiles whose document ids can match (or null)
   int nq_doc, nk_doc;
+  // Document masks: [B][n_ctas] CTA indices, longest first (or null); the
+  // grid is then (n_ctas * Hq, 1, B) with heads fastest.
+  const int* cta_order;
   // Ring accumulation (acc_o non-null): the launch's normalised rows are
   // folded into a running result by log-sum-exp (the per-step update of
   // ring_attention, attnax/kernels/attention.py:662-671) instead of being
@@ -115,8 +118,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sp = smem_raw + (sb - raw_base);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ct = a.n_ctas - 1 - (int)blockIdx.x;  // heavy (late) tiles first
-  const int hq = blockIdx.y, b = blockIdx.z;
+  const int b = blockIdx.z;
+  int ct, hq;
+  if (a.cta_order) {
+    const int k = (int)blockIdx.x / a.Hq;
+    hq = (int)blockIdx.x - k * a.Hq;
+    ct = a.cta_order[(long long)b * a.n_ctas + k];
+  } else {
+    ct = a.n_ctas - 1 - (int)blockIdx.x;  // heavy (late) tiles first
+    hq = blockIdx.y;
+  }
   const int hkv = hq / a.group;
   int q0[2], q1[2];
   bool act[2];

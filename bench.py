@@ -311,9 +311,10 @@ def run_flash(args, torch, dist, rank, world, peaks):
 
 # Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of each
 # phase at the B4 bench size: ncu capture of the B1 case of the same workload
-# (profiles/flash_bwd_kernels_small.md) x 4 batches.  fwd: flash_fwd2_kernel
-# 133.2 MB; bwd: prep_rows 222.7 MB + fused dkdv 427.7 MB + dq_convert 176.3 MB.
-TRAFFIC = {"fwd": 4 * 133.2e6, "bwd": 4 * (222.7e6 + 427.7e6 + 176.3e6)}
+# (profiles/flash_fwd2_kernel_small.md, profiles/flash_bwd_kernels_small.md) x 4
+# batches.  fwd: flash_fwd2_kernel 134.5 MB; bwd: prep_rows 222.7 MB + fused dkdv
+# 428.2 MB + dq_convert 176.3 MB.
+TRAFFIC = {"fwd": 4 * 134.5e6, "bwd": 4 * (222.7e6 + 428.2e6 + 176.3e6)}
 # Paged decode: DRAM bytes / algorithmic bytes of the 16-sequence capture
 # (profiles/paged_decode_kernel_small.md); traffic scales with the tokens read.
 PAGED_TRAFFIC_RATIO = (1.100622e9 + 6.36672e6) / 1.1001e9
