@@ -563,6 +563,13 @@ static int launch_sm100_bwd(const attn_bwd_params_t* p, float* delta, float* lse
       // dQ accumulated in fp32 by the dK/dV kernel, then scaled and converted.
       static int attr_dev_f = -1;
       auto kf = dkdv_kernel<D, BF16, true>;
+      if (attr_dev_f < 0 && CfgKV<D, true>::DQW) {
+        // The in-kernel setmaxnreg split draws on exactly LAUNCH_REGS registers per
+        // thread: with any other launch count the growing warps could wait forever.
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, kf) != cudaSuccess || fa.numRegs != CfgKV<D, true>::LAUNCH_REGS)
+          return ATTN_ERR_UNSUPPORTED;
+      }
       if (!smem_attr_once(kf, CfgKV<D, true>::SMEM, &attr_dev_f)) return ATTN_ERR_CUDA;
       // (dq_acc rows were zeroed by prep_rows_kernel; the transposed layout is cleared here)
       if (CfgKV<D, true>::RED &&

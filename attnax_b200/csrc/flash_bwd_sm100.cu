@@ -84,6 +84,10 @@ constexpr int QROWS = 128;  // q rows per dq CTA (MMA M)
 #ifndef ATTN_BWD_DQ_STEPS
 #define ATTN_BWD_DQ_STEPS 1   // fused kernel: 1 = one staged bulk add per tile, else one per column group
 #endif
+#ifndef ATTN_BWD_DQ_WARPS
+#define ATTN_BWD_DQ_WARPS 1   // fused kernel: a warpgroup of its own reads dQ^T out of TMEM and stages it
+                              // (traced: on the elementwise warps it took ~0.54 us of a ~1.75 us iteration)
+#endif
 constexpr int KT = ATTN_BWD_DQ_KT;  // kv rows per dq iteration (MMA N): 64 or 128
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -186,7 +190,6 @@ struct CfgKV {
   static constexpr int SPLIT = FQ_STAGED ? ATTN_BWD_EW_SPLIT : 2;
   static_assert(SPLIT == 2 || SPLIT == 4, "elementwise split");
   static constexpr int EW_WARPS = 4 * SPLIT;
-  static constexpr int THREADS = (EW_WARPS + 2) * 32;  // + TMA warp + MMA warp
   static constexpr int HC = QT / SPLIT;                // columns per elementwise thread
   static constexpr int OFF_COLV = OFF_DS + PB * KROWS * 128;  // per elementwise warp: 32 column terms
   // Fused dQ staging [QT / DQ_STEPS q][D] fp32: with one step every column
@@ -194,6 +197,18 @@ struct CfgKV {
   // steps the groups take turns on a buffer of HC rows.
   static constexpr int DQ_STEPS = ATTN_BWD_DQ_STEPS == 1 ? 1 : SPLIT;
   static constexpr int DQ_ROWS = QT / DQ_STEPS;
+  // Dedicated dQ warpgroup (warps EW_WARPS .. EW_WARPS + 3, one per TMEM lane
+  // quarter = 32 head-dim rows of dQ^T), then the TMA and MMA warps and two
+  // idle warps completing their warpgroup: 16 warps launched at 128
+  // registers, split by setmaxnreg as 256 * EW_REGS + 128 * DQ_REGS +
+  // 128 * TM_REGS == 512 * LAUNCH_REGS.  Otherwise the elementwise warps
+  // flush dQ^T themselves and the CTA is EW_WARPS + 2 warps.
+  static constexpr bool DQW = FQ_STAGED && DQ_STEPS == 1 && SPLIT == 2 && ATTN_BWD_DQ_WARPS != 0;
+  static constexpr int TMA_WARP = DQW ? EW_WARPS + 4 : EW_WARPS;
+  static constexpr int MMA_WARP = TMA_WARP + 1;
+  static constexpr int THREADS = DQW ? 512 : (EW_WARPS + 2) * 32;
+  static constexpr int LAUNCH_REGS = 128, EW_REGS = 168, DQ_REGS = 96, TM_REGS = 80;
+  static_assert(!DQW || 256 * EW_REGS + 128 * DQ_REGS + 128 * TM_REGS == 512 * LAUNCH_REGS, "register split");
   // With V in TMEM its shared-memory tile is dead once the elementwise warps
   // have copied it (before the MMA warp issues anything), so the one-step
   // staging buffer (QT x D fp32 = one V tile) reuses it.
@@ -279,13 +294,13 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
     mbar_init(kv_tmem, C::EW_WARPS);
     for (int x = 0; x < 2; ++x) {
       mbar_init(dq_full(x), 1);
-      mbar_init(dq_free(x), C::EW_WARPS);
+      mbar_init(dq_free(x), C::DQW ? 4 : C::EW_WARPS);
     }
-    mbar_init(stage_full, C::EW_WARPS / C::DQ_STEPS);  // the warps staging one step
+    mbar_init(stage_full, C::DQW ? 4 : C::EW_WARPS / C::DQ_STEPS);  // the warps staging one step
     mbar_init(stage_free, 1);
     fence_mbar_init();
   }
-  if (warp == C::EW_WARPS + 1) {
+  if (warp == C::MMA_WARP) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -315,7 +330,12 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
   // (g, qt) advance of the flat (g, q tile) loop.
 #define DKDV_NEXT(g, qt) ((qt) + 1 == t_hi ? ((qt) = t_lo, ++(g)) : ++(qt))
 
-  if (warp == C::EW_WARPS) {
+  // With the dQ warpgroup, each role branch starts with its setmaxnreg (whole
+  // warpgroups, as the instruction requires: the TMA/MMA branch also holds
+  // the two idle warps), so the register budget covers that role's code.
+  if (warp >= C::TMA_WARP) {
+   if constexpr (C::DQW) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::TM_REGS));
+   if (warp == C::TMA_WARP) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -344,7 +364,7 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
         ++i;
       }
     }
-  } else if (warp == C::EW_WARPS + 1) {
+   } else if (warp == C::MMA_WARP) {
     if (lane == 0) {
       constexpr int FMT = BF16 ? 1 : 0;
       constexpr uint32_t ID_S = idesc_f16(128, QT, FMT, 0, 0);
@@ -422,7 +442,9 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
       if (ok && i > 0) ok = issue_grads(i - 1);
       umma_commit(acc_done);
     }
+   }
   } else if (warp < C::EW_WARPS) {
+    if constexpr (C::DQW) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::EW_REGS));
     const int r = threadIdx.x & 127;  // kv row within the tile == TMEM lane
     const int half = warp >> 2;       // columns [HC*half, HC*half + HC) of each q tile
     constexpr int HC = C::HC;
@@ -646,7 +668,7 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive_warp(p_full);
-      if (FQ && i > 0) {
+      if (FQ && !C::DQW && i > 0) {
         ok = flush_dq(i - 1, prev_hq, prev_q0);
         if (!ok) break;
       }
@@ -654,8 +676,8 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
       prev_q0 = q0;
       ++i;
     }
-    if (FQ && ok && i > 0) ok = flush_dq(i - 1, prev_hq, prev_q0);
-    if (FQ && threadIdx.x == 0) bulk_wait_all();
+    if (FQ && !C::DQW && ok && i > 0) ok = flush_dq(i - 1, prev_hq, prev_q0);
+    if (FQ && !C::DQW && threadIdx.x == 0) bulk_wait_all();
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, kStatusTimeoutSoftmax));
     if (ok) {
       tc_fence_after();
@@ -694,10 +716,62 @@ __global__ void __launch_bounds__(CfgKV<D, FQ>::THREADS, 1)
         }
       }
     }
+  } else if (C::DQW && warp < C::EW_WARPS + 4) {
+    if constexpr (C::DQW) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::DQ_REGS));
+    // ------------------------------------------------------------ dQ^T out --
+    // Tile j's dQ^T (this thread: head-dim row r, all QT q columns) -> staging
+    // [QT q][D] fp32 in the dead V tile -> one bulk add of the block into
+    // dq_acc by the group's first thread, once the previous bulk add has read
+    // the staging buffer.  Same (g, q tile) walk and skips as the other roles.
+    const int r = threadIdx.x & 127;  // head-dim row of dQ^T == TMEM lane
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const bool leader = threadIdx.x == C::EW_WARPS * 32;
+    float* stg = reinterpret_cast<float*>(sp + C::OFF_DQS);
+    bool ok = true;
+    int j = 0;
+    for (int it = 0, g = 0, qt = t_lo; it < iters; ++it, DKDV_NEXT(g, qt)) {
+      if (state_of(qt) == kSkip) continue;
+      const int hq = hkv * a.group + g, q0 = qt * QT;
+      ok = __all_sync(0xffffffffu, mbar_wait(dq_full(j % C::NDQ), (j / C::NDQ) & 1, kStatusTimeoutSoftmax));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tmem + lane_base + C::COL_DQ + (j % C::NDQ) * QT, v0);
+      tmem_ld32(tmem + lane_base + C::COL_DQ + (j % C::NDQ) * QT + 32, v1);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive_warp(dq_free(j % C::NDQ));
+      const uint32_t ph = (uint32_t)j & 1u;
+      if (leader) {
+        bulk_wait_read_all();  // the previous reduction has read the staging buffer
+        mbar_arrive(stage_free);
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(stage_free, ph, kStatusTimeoutSoftmax));
+      if (!ok) break;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        stg[c * D + r] = __uint_as_float(v0[c]);
+        stg[(c + 32) * D + r] = __uint_as_float(v1[c]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive_warp(stage_full);
+      if (leader) {
+        ok = mbar_wait(stage_full, ph, kStatusTimeoutSoftmax);
+        if (ok) {
+          bulk_reduce_add_f32(a.dq_acc + (((long long)b * a.Hq + hq) * a.Sq_pad + q0) * D, smem_u32(stg),
+                              QT * D * 4);
+          bulk_commit();
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      ++j;
+    }
+    if (leader) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == C::EW_WARPS + 1) {
+  if (warp == C::MMA_WARP) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
