@@ -68,9 +68,14 @@ def release_comms():
 
 
 def _comm_stream(device):
+    """The stream of the ring's NCCL transfers, at the highest priority: the
+    attention kernel of a hop fills every SM, and the block scheduler hands
+    SMs that free up to the higher-priority stream's CTAs first, so the next
+    hop's K/V transfer starts during this hop instead of after its last wave."""
     s = _STREAMS.get(device.index)
     if s is None:
-        s = _STREAMS[device.index] = torch.cuda.Stream(device=device)
+        lo, hi = torch.cuda.Stream.priority_range() if hasattr(torch.cuda.Stream, "priority_range") else (0, -1)
+        s = _STREAMS[device.index] = torch.cuda.Stream(device=device, priority=min(lo, hi))
     return s
 
 
