@@ -39,6 +39,7 @@ struct NcclFns {
   decltype(&ncclRecv) recv = nullptr;
   decltype(&ncclGroupStart) group_start = nullptr;
   decltype(&ncclGroupEnd) group_end = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
 };
 
@@ -62,10 +63,11 @@ static const NcclFns* nccl() {
     ATTN_NCCL_SYM(recv, "ncclRecv");
     ATTN_NCCL_SYM(group_start, "ncclGroupStart");
     ATTN_NCCL_SYM(group_end, "ncclGroupEnd");
+    ATTN_NCCL_SYM(all_gather, "ncclAllGather");
     ATTN_NCCL_SYM(error_string, "ncclGetErrorString");
 #undef ATTN_NCCL_SYM
     ok = f.get_unique_id && f.init_rank && f.destroy && f.send && f.recv && f.group_start && f.group_end &&
-         f.error_string;
+         f.all_gather && f.error_string;
   });
   return ok ? &f : nullptr;
 }
@@ -236,7 +238,138 @@ struct attn_comm_s {
   ncclComm_t comm;
   int world, rank, device;
   cudaEvent_t ev[8];
+  // Copy-engine K/V rotation (attnb200::ringhost::ce_ensure): two receive
+  // slots of ce_slot bytes and a flags page of this rank, IPC-shared; the
+  // next rank's slots and flags opened here.  Flags: [0] ready = hops whose
+  // K/V have landed in this rank's slots, [kFlagDone] done = hops this rank
+  // has finished with (compute and outgoing copy); both only grow, counted
+  // from ce_epoch, which every rank advances alike.
+  int ce_state = 0;  // 0 not set up, 1 in use, -1 unavailable (NCCL rotation)
+  char* ce_buf = nullptr;
+  size_t ce_slot = 0;
+  unsigned long long* ce_flags = nullptr;
+  char* ce_peer_buf = nullptr;
+  unsigned long long* ce_peer_flags = nullptr;
+  unsigned long long ce_epoch = 0;
 };
+
+namespace attnb200 {
+namespace ringhost {
+
+constexpr int kFlagDone = 16;          // done counter one 128-byte line after ready
+constexpr size_t kFlagBytes = 256;
+
+// Waits (one thread) until *flag >= target; gives up after ATTN_WAIT_NS, or
+// when another wait already failed, recording a status code instead.
+__global__ void ce_wait_kernel(const unsigned long long* flag, unsigned long long target) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    if (v >= target) return;
+    if (status_now() != 0) return;
+    if (globaltimer() - t0 > ATTN_WAIT_NS) {
+      atomicCAS(&g_status, 0, kStatusTimeoutOther);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+// *flag = value with release semantics at system scope (flag may be a peer's):
+// everything this stream did before -- a copy into the peer's slot -- is
+// visible to whoever acquires the new value.
+__global__ void ce_signal_kernel(unsigned long long* flag, unsigned long long value) {
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(value) : "memory");
+}
+
+// All-gather of one fixed-size host record per rank through the comm (setup
+// only: synchronous).
+static int ce_all_gather(attn_comm_s* c, const void* rec, size_t bytes, void* all, cudaStream_t st) {
+  const NcclFns* f = nccl();
+  char* d = nullptr;
+  if (cudaMalloc(&d, bytes * (c->world + 1)) != cudaSuccess) return ATTN_ERR_CUDA;
+  int rc = ATTN_OK;
+  if (cudaMemcpyAsync(d, rec, bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) rc = ATTN_ERR_CUDA;
+  if (rc == ATTN_OK) rc = nccl_status(f->all_gather(d, d + bytes, bytes, ncclUint8, c->comm, st), "ncclAllGather");
+  if (rc == ATTN_OK && cudaMemcpyAsync(all, d + bytes, bytes * c->world, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    rc = ATTN_ERR_CUDA;
+  if (rc == ATTN_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = ATTN_ERR_CUDA;
+  cudaFree(d);
+  return rc;
+}
+
+static void ce_release(attn_comm_s* c) {
+  if (c->ce_peer_buf) cudaIpcCloseMemHandle(c->ce_peer_buf);
+  if (c->ce_peer_flags) cudaIpcCloseMemHandle(c->ce_peer_flags);
+  if (c->ce_buf) cudaFree(c->ce_buf);
+  c->ce_peer_buf = nullptr;
+  c->ce_peer_flags = nullptr;
+  c->ce_buf = nullptr;
+  c->ce_slot = 0;
+}
+
+// Makes the copy-engine rotation ready for slots of `slot` bytes: a collective
+// call (every rank of the comm, same sizes, same order).  Returns ATTN_OK with
+// c->ce_state == 1 when every rank has its slots and its next rank's slots
+// and flags mapped, ATTN_OK with ce_state == -1 when some rank could not (the
+// caller then rotates with NCCL), or an error code.
+static int ce_ensure(attn_comm_s* c, size_t slot, cudaStream_t st) {
+  if (c->world < 2 || c->ce_state < 0) return ATTN_OK;
+  if (c->ce_state == 1 && slot <= c->ce_slot) return ATTN_OK;
+  // Nobody may still be copying into or reading the old slots.
+  if (cudaDeviceSynchronize() != cudaSuccess) return ATTN_ERR_CUDA;
+  struct Rec {
+    cudaIpcMemHandle_t buf, flags;
+    int ok;
+  } mine{}, *all = new Rec[c->world];
+  int rc = ce_all_gather(c, &mine, sizeof(Rec), all, st);  // barrier: every rank is past its old slots
+  if (rc != ATTN_OK) {
+    delete[] all;
+    return rc;
+  }
+  ce_release(c);
+  bool ok = true;
+  if (!c->ce_flags) {
+    ok = cudaMalloc(&c->ce_flags, kFlagBytes) == cudaSuccess && cudaMemset(c->ce_flags, 0, kFlagBytes) == cudaSuccess;
+    if (!ok) c->ce_flags = nullptr;
+  }
+  ok = ok && cudaMalloc(&c->ce_buf, 2 * slot) == cudaSuccess;
+  ok = ok && cudaIpcGetMemHandle(&mine.buf, c->ce_buf) == cudaSuccess;
+  ok = ok && cudaIpcGetMemHandle(&mine.flags, c->ce_flags) == cudaSuccess;
+  mine.ok = ok ? 1 : 0;
+  rc = ce_all_gather(c, &mine, sizeof(Rec), all, st);
+  if (rc == ATTN_OK && ok) {
+    const Rec& nx = all[(c->rank + 1) % c->world];
+    void* pb = nullptr;
+    void* pf = nullptr;
+    ok = nx.ok && cudaIpcOpenMemHandle(&pb, nx.buf, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    if (ok) c->ce_peer_buf = static_cast<char*>(pb);
+    ok = ok && cudaIpcOpenMemHandle(&pf, nx.flags, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    if (ok) c->ce_peer_flags = static_cast<unsigned long long*>(pf);
+  }
+  cudaGetLastError();  // a failed IPC call is answered below, not left pending
+  // Every rank must take the same rotation: agree on the outcome.
+  mine.ok = (rc == ATTN_OK && ok) ? 1 : 0;
+  if (rc == ATTN_OK) rc = ce_all_gather(c, &mine, sizeof(Rec), all, st);
+  bool all_ok = rc == ATTN_OK;
+  for (int i = 0; all_ok && i < c->world; ++i) all_ok = all[i].ok != 0;
+  delete[] all;
+  if (rc != ATTN_OK) return rc;
+  if (!all_ok) {
+    ce_release(c);
+    c->ce_state = -1;
+    fprintf(stderr, "attnb200: ring K/V over copy engines unavailable; rotating with NCCL\n");
+    return ATTN_OK;
+  }
+  c->ce_slot = slot;
+  c->ce_state = 1;
+  return ATTN_OK;
+}
+
+}  // namespace ringhost
+}  // namespace attnb200
 
 extern "C" {
 
@@ -287,6 +420,8 @@ int attn_comm_destroy(attn_comm_t c) {
   if (!c) return ATTN_ERR_INVALID;
   const NcclFns* f = nccl();
   int rc = ATTN_OK;
+  ce_release(c);
+  if (c->ce_flags) cudaFree(c->ce_flags);
   if (f) rc = nccl_status(f->destroy(c->comm), "ncclCommDestroy");
   for (auto& e : c->ev) cudaEventDestroy(e);
   delete c;
@@ -395,7 +530,15 @@ extern "C" int attn_ring_fwd(const attn_ring_params_t* p, attn_comm_t comm, void
   const int C = zig ? (int)(S / 2) : (int)S;
   const size_t row = D * es;
   const size_t kv_plane = B * Hkv * S * D * es;
-  char* kvb[2] = {ws + w.kv0, ws + w.kv1};
+  // K/V slots: the copy-engine rotation's IPC-shared slots when every rank
+  // has them (the next hop's K/V goes straight into the next rank's slot
+  // with cudaMemcpyAsync, no SMs), else the workspace with NCCL send/recv.
+  {
+    const int crc = ce_ensure(comm, 2 * kv_plane, ms);
+    if (crc != ATTN_OK) return crc;
+  }
+  const bool ce = P > 1 && comm->ce_state == 1;
+  char* kvb[2] = {ce ? comm->ce_buf : ws + w.kv0, ce ? comm->ce_buf + comm->ce_slot : ws + w.kv1};
   float* o_acc = reinterpret_cast<float*>(ws + w.o_acc);
   float* lse_acc = reinterpret_cast<float*>(ws + w.lse_acc);
   void* qbuf = zig ? static_cast<void*>(ws + w.q) : const_cast<void*>(p->q);
@@ -463,18 +606,38 @@ extern "C" int attn_ring_fwd(const attn_ring_params_t* p, attn_comm_t comm, void
   const std::vector<Launch> L = plan(s, position_free);
   size_t n = 0;
   bool redeal_waited = !zig;
+  // Copy-engine counters of this call: hop i's K/V has landed in a rank's
+  // slot i&1 when its ready >= base + i; a rank is done with hop i (compute
+  // and its outgoing copy) when its done >= base + i + 1.
+  const unsigned long long base = comm->ce_epoch;
+  if (ce) comm->ce_epoch += P;
   for (int i = 0; i < P; ++i) {
-    // start moving this hop's K/V on to rank r+1 (the buffer it lands in was
-    // last read by hop i-1)
+    // start moving this hop's K/V on to rank r+1
     if (i + 1 < P) {
       // (the re-deal's rows were written on the comm stream itself)
       if (i == 0) ATTN_CK(cudaStreamWaitEvent(ms, ev_local, 0));
-      if (i > 0) ATTN_CK(cudaStreamWaitEvent(ms, ev_hop[(i - 1) & 1], 0));
-      ATTN_NK(f->group_start(), "ncclGroupStart");
-      ATTN_NK(f->send(kvb[i & 1], 2 * kv_plane, u8, (r + 1) % P, comm->comm, ms), "ncclSend");
-      ATTN_NK(f->recv(kvb[(i + 1) & 1], 2 * kv_plane, u8, (r - 1 + P) % P, comm->comm, ms), "ncclRecv");
-      ATTN_NK(f->group_end(), "ncclGroupEnd");
-      ATTN_CK(cudaEventRecord(ev_recv[i & 1], ms));
+      if (ce) {
+        // slot i&1 holds this hop's K/V once it has landed (hop 0: own rows);
+        // rank r+1's slot (i+1)&1 is free once it is done with hop i-1
+        if (i > 0) ce_wait_kernel<<<1, 1, 0, ms>>>(comm->ce_flags, base + i);
+        ce_wait_kernel<<<1, 1, 0, ms>>>(comm->ce_peer_flags + kFlagDone, base + i);
+        ATTN_CK(cudaMemcpyAsync(comm->ce_peer_buf + ((i + 1) & 1) * comm->ce_slot, kvb[i & 1], 2 * kv_plane,
+                                cudaMemcpyDeviceToDevice, ms));
+        ce_signal_kernel<<<1, 1, 0, ms>>>(comm->ce_peer_flags, base + i + 1);
+        if ((rc = launch_status(i > 0 ? 3 : 2)) != ATTN_OK) return rc;
+      } else {
+        // (the buffer it lands in was last read by hop i-1)
+        if (i > 0) ATTN_CK(cudaStreamWaitEvent(ms, ev_hop[(i - 1) & 1], 0));
+        ATTN_NK(f->group_start(), "ncclGroupStart");
+        ATTN_NK(f->send(kvb[i & 1], 2 * kv_plane, u8, (r + 1) % P, comm->comm, ms), "ncclSend");
+        ATTN_NK(f->recv(kvb[(i + 1) & 1], 2 * kv_plane, u8, (r - 1 + P) % P, comm->comm, ms), "ncclRecv");
+        ATTN_NK(f->group_end(), "ncclGroupEnd");
+      }
+      ATTN_CK(cudaEventRecord(ev_recv[i & 1], ms));  // CE: this hop's outgoing copy; NCCL: next hop's K/V
+    }
+    if (ce && i > 0) {
+      ce_wait_kernel<<<1, 1, 0, cs>>>(comm->ce_flags, base + i);  // this hop's K/V has landed
+      if ((rc = launch_status()) != ATTN_OK) return rc;
     }
     for (; n < L.size() && L[n].hop == i; ++n) {
       if (!L[n].local && !redeal_waited) {
@@ -486,6 +649,10 @@ extern "C" int attn_ring_fwd(const attn_ring_params_t* p, attn_comm_t comm, void
     }
     ATTN_CK(cudaEventRecord(ev_hop[i & 1], cs));
     if (i + 1 < P) ATTN_CK(cudaStreamWaitEvent(cs, ev_recv[i & 1], 0));
+    if (ce) {
+      ce_signal_kernel<<<1, 1, 0, cs>>>(comm->ce_flags + kFlagDone, base + i + 1);
+      if ((rc = launch_status()) != ATTN_OK) return rc;
+    }
   }
 
   // ---- results back to the public layout ----
