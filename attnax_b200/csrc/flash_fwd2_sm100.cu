@@ -104,6 +104,44 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return __int_as_float(__float_as_int(p) + ((__float_as_int(y) - 0x4B400000) << 23));
 }
 
+// Boundary tile of a band, prefix or document mask: this thread's row of S in
+// TMEM (s_addr, BN columns) gets -inf in every dropped column, 32 columns at a
+// time.  dq0 = q - kv and kv0 = global kv at column 0; ncols columns lie inside
+// the sequence; doc_ids (or null) holds the tile's column document ids.  Out
+// of line, so the full-tile code around the call keeps its registers and
+// schedule.
+__device__ __noinline__ void mask_boundary_row(uint32_t s_addr, long long dq0, long long kv0, int ncols, bool has_band,
+                                               long long band_lo, long long band_hi, bool has_prefix, int pref,
+                                               const int* doc_ids, int doc_row) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t raw[32];
+    tmem_ld32(s_addr + c * 32, raw);
+    const long long dc = dq0 - c * 32;  // q - kv at chunk column e is dc - e
+    uint32_t keep = bit_range(0, (long long)ncols - c * 32 - 1);  // inside the sequence
+    if (has_band) keep &= bit_range(dc - band_hi, dc - band_lo);
+    if (has_prefix) keep &= bit_range(0, pref - (kv0 + c * 32) - 1) | bit_range(0, dc);
+    if (doc_ids) {
+      const int4* ids = reinterpret_cast<const int4*>(doc_ids + c * 32);
+      uint32_t same = 0u;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int4 v = ids[u];
+        same |= ((uint32_t)(v.x == doc_row) | ((uint32_t)(v.y == doc_row) << 1) | ((uint32_t)(v.z == doc_row) << 2) |
+                 ((uint32_t)(v.w == doc_row) << 3))
+                << (4 * u);
+      }
+      keep &= same;
+    }
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if (!((keep >> e) & 1u)) raw[e] = 0xff800000u;  // -inf
+    tmem_st32(s_addr + c * 32, raw);
+  }
+  tmem_wait_st();
+}
+
 // ACC: the ring variant that merges into a running result (Args::acc_o); a
 // separate instantiation so the plain forward's epilogue stays as it is.
 template <int D, bool BF16, bool ACC = false>
@@ -372,36 +410,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int u = 0; u < BN / 32; ++u) doc_ids[u * 32 + lane] = cid[u];
           __syncwarp();
         }
-        // q - kv of this row at column 0 of the tile (global positions)
-        const long long dq0 = qg_row - (a.mask.kv_offset + k0);
-        const long long kv0 = a.mask.kv_offset + k0;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t raw[32];
-          tmem_ld32(s_addr + c * 32, raw);
-          const long long dc = dq0 - c * 32;  // q - kv at chunk column e is dc - e
-          uint32_t keep = bit_range(0, (long long)a.Skv - k0 - c * 32 - 1);  // inside the sequence
-          if (a.mask.has_band) keep &= bit_range(dc - a.mask.band_hi, dc - a.mask.band_lo);
-          if (a.mask.prefix_len) keep &= bit_range(0, pref - (kv0 + c * 32) - 1) | bit_range(0, dc);
-          if (has_doc) {
-            const int4* ids = reinterpret_cast<const int4*>(doc_ids + c * 32);
-            uint32_t same = 0u;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int4 v = ids[u];
-              same |= ((uint32_t)(v.x == doc_row) | ((uint32_t)(v.y == doc_row) << 1) |
-                       ((uint32_t)(v.z == doc_row) << 2) | ((uint32_t)(v.w == doc_row) << 3))
-                      << (4 * u);
-            }
-            keep &= same;
-          }
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (!((keep >> e) & 1u)) raw[e] = 0xff800000u;  // -inf
-          tmem_st32(s_addr + c * 32, raw);
-        }
-        tmem_wait_st();
+        mask_boundary_row(s_addr, qg_row - (a.mask.kv_offset + k0), a.mask.kv_offset + k0, a.Skv - k0,
+                          a.mask.has_band != 0, a.mask.band_lo, a.mask.band_hi, a.mask.prefix_len != nullptr, pref,
+                          has_doc ? doc_ids : nullptr, doc_row);
       } else if (part) {
         // Boundary tile: mask/transform 32 columns at a time in TMEM so the
         // per-column mask state never competes with the 128 scores.
