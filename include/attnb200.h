@@ -228,8 +228,18 @@ typedef struct {
 
 size_t attn_ring_fwd_workspace_size(const attn_ring_params_t* p, int32_t world);
 /* Enqueues the whole ring on compute_stream (attention) and comm_stream
- * (NCCL); the results are ready in stream order of compute_stream.  Every
- * rank of the communicator must call it with the same shapes and band. */
+ * (transfers); the results are ready in stream order of compute_stream.
+ * Every rank of the communicator must call it with the same shapes and band.
+ * The per-hop K/V rotation runs on the copy engines: the communicator owns
+ * two receive slots of 2 x K/V shard bytes and a flags page on each rank,
+ * shared with the previous rank through CUDA IPC.  The first call, and any
+ * later call that needs larger slots, sets them up collectively: it
+ * synchronizes the device, allocates with cudaMalloc and exchanges handles
+ * over NCCL, so that call must be made by all ranks and outside any stream
+ * capture.  If any rank cannot map its neighbour's slots (no peer access, or
+ * two ranks on one GPU), all ranks rotate with NCCL send/recv instead.  A
+ * higher-priority comm_stream lets its work start while the attention
+ * kernels hold every SM.  attn_comm_destroy frees the slots. */
 int attn_ring_fwd(const attn_ring_params_t* p, attn_comm_t comm, void* compute_stream, void* comm_stream);
 
 /* Gradients of attn_ring_fwd (the reference differentiates its lax.scan /
