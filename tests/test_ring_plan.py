@@ -126,3 +126,14 @@ def test_ring_plan_balances_causal_work():
                         n += int(np.sum(ki <= qi))
             per_rank.append(n)
         assert len(set(per_rank)) == 1, (hop, per_rank)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ring_plan_batches_q_chunks_only_in_final_launches(world):
+    """A launch over both q chunks writes their finished rows (final_from 0):
+    the batched shape that folds rows into the fp32 running result measured
+    slower than two separate launches, so the plan never issues it."""
+    for r in range(world):
+        for l in _ring_capi.plan(world, r, 64, True, (0, BAND_INF), position_free=True):
+            if l["q_chunks"] == 2:
+                assert l["final_from"] == 0, (world, r, l)
